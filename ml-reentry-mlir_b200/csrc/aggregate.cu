@@ -1,0 +1,808 @@
+// CSR aggregation kernels for sm_100a: GCNConv's weighted SpMM and GATConv's
+// fused SDDMM -> LeakyReLU -> edge softmax -> SpMM, plus the degree-skew plan.
+//
+// Reference semantics (PyG eager, as captured op by op in
+// experiments/gatconv/dumps/gat.1-raw-torch.mlir:25-129):
+//   e_k  = leaky_relu(asrc[src_k] + adst[dst_k], 0.2)           (:25-38)
+//   m    = scatter_amax_dst(e)  (include_self = false)           (:56-60)
+//   p_k  = exp(e_k - m[dst_k])                                    (:61-65)
+//   S    = scatter_add_dst(p) + 1e-16                             (:82-87)
+//   out  = scatter_add_dst(p_k / S[dst_k] * h[src_k])             (:88-125)
+// and for GCN the sparsifier's CSR row loop out[i] = sum_k w_k h[col_k]
+// (test/reference/gcn.linalg-on-tensors.mlir:20, gnnc/schedule/sparse.py:47-62).
+//
+// Layout and schedule
+//  * One warp owns one destination row (rows of degree <= cta_threshold).
+//    Edges are taken 32 at a time: lane l loads col[k+l] and the edge's
+//    logits, the warp reduces the per-head max / exp-sum with shuffles
+//    (online across 32-edge chunks), and the chunk's (src, p) pairs go to
+//    shared memory. The warp then streams the h[src] rows: each lane loads a
+//    16-byte vector (8 bf16 or 4 fp32 features) of every row, so one edge is
+//    one fully coalesced row read; loads are unrolled for memory-level
+//    parallelism. Logits never leave the SM.
+//  * Rows longer than cta_threshold are processed by a whole CTA (its warps
+//    split the edge range and combine (max, sum, acc) in shared memory).
+//    Rows longer than split_threshold are cut into segments processed by
+//    different CTAs; each writes a partial (max, sum, acc) and a merge kernel
+//    combines them in slot order, so results are deterministic (no float
+//    atomics anywhere).
+//  * The grid is persistent (a multiple of the SM count). CTAs first drain the
+//    CTA work list (largest items first), then every warp pulls contiguous,
+//    edge-balanced row ranges from a second list.
+//  * Epilogue, fused: divide by the softmax denominator, concat or mean over
+//    heads, + bias, ReLU / ELU, optional row log_softmax, convert, store.
+#include <algorithm>
+#include <vector>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kHMax = 16;
+constexpr unsigned kFull = 0xffffffffu;
+
+enum AggMode { MODE_GCN = 0, MODE_GAT = 1, MODE_SCORES = 2 };
+
+struct AggParams {
+  const int32_t* rowptr;
+  const int32_t* col;
+  const float* w;       // GCN edge values [E]
+  const float* asrc;    // GAT [n_src, H]
+  const float* adst;    // GAT [n_rows, H]
+  const float* scores;  // MODE_SCORES [E, H]
+  const void* h;
+  int64_t ldh;  // elements
+  int64_t n_rows, n_src;
+  int64_t e_lo, e_hi;  // valid edge index range (from the plan's rowptr)
+  int H, C, F, F_pad, HS;
+  float slope, eps;
+  int mode, concat, act, log_softmax;
+  const float* bias;
+  void* out;
+  int out_dtype;
+  int64_t ldo;
+  int F_out;
+  const int4* cta_items;
+  int64_t n_cta_items;
+  const int4* split_rows;
+  const int32_t* warp_tasks;
+  int64_t n_warp_tasks;
+  int cta_threshold;
+  float* partials;
+  int part_stride;
+  int* counters;  // [0] next CTA item, [1] next warp task, [2] bad-index flag
+};
+
+template <typename TH, int VEC>
+struct VecLoad;
+
+template <>
+struct VecLoad<float, 4> {
+  static __device__ __forceinline__ void run(const char* p, float* d) {
+    float4 v = __ldg(reinterpret_cast<const float4*>(p));
+    d[0] = v.x; d[1] = v.y; d[2] = v.z; d[3] = v.w;
+  }
+};
+template <>
+struct VecLoad<float, 1> {
+  static __device__ __forceinline__ void run(const char* p, float* d) {
+    d[0] = __ldg(reinterpret_cast<const float*>(p));
+  }
+};
+template <>
+struct VecLoad<__nv_bfloat16, 8> {
+  static __device__ __forceinline__ void run(const char* p, float* d) {
+    uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+    d[0] = bf16_lo(v.x); d[1] = bf16_hi(v.x); d[2] = bf16_lo(v.y); d[3] = bf16_hi(v.y);
+    d[4] = bf16_lo(v.z); d[5] = bf16_hi(v.z); d[6] = bf16_lo(v.w); d[7] = bf16_hi(v.w);
+  }
+};
+template <>
+struct VecLoad<__nv_bfloat16, 1> {
+  static __device__ __forceinline__ void run(const char* p, float* d) {
+    unsigned short v = __ldg(reinterpret_cast<const unsigned short*>(p));
+    d[0] = __uint_as_float(uint32_t(v) << 16);
+  }
+};
+
+__device__ __forceinline__ float apply_act(float v, int act) {
+  if (act == GNNC_ACT_RELU) return fmaxf(v, 0.f);
+  if (act == GNNC_ACT_ELU) return v > 0.f ? v : expm1f(v);
+  return v;
+}
+
+// Final value of output feature c from the aggregated [H*C] row in smem.
+__device__ __forceinline__ float out_value(const AggParams& p, const float* s_row, int c) {
+  float v;
+  if (p.concat) {
+    v = s_row[c];
+  } else {
+    v = 0.f;
+    for (int hd = 0; hd < p.H; ++hd) v += s_row[hd * p.C + c];
+    v = v / float(p.H);
+  }
+  if (p.bias) v += __ldg(p.bias + c);
+  return apply_act(v, p.act);
+}
+
+// Epilogue for one row, run by one full warp. s_row holds the aggregated
+// (already normalised) [F] values.
+__device__ void warp_epilogue(const AggParams& p, int64_t row, const float* s_row, int lane) {
+  const int Fo = p.F_out;
+  float mx = 0.f, lse = 0.f;
+  if (p.log_softmax) {
+    float m = -INFINITY;
+    for (int c = lane; c < Fo; c += 32) m = fmaxf(m, out_value(p, s_row, c));
+    mx = warp_max(m);
+    float se = 0.f;
+    for (int c = lane; c < Fo; c += 32) se += expf(out_value(p, s_row, c) - mx);
+    lse = logf(warp_sum(se));
+  }
+  const size_t base = size_t(row) * size_t(p.ldo);
+  for (int c = lane; c < Fo; c += 32) {
+    float v = out_value(p, s_row, c);
+    if (p.log_softmax) v = (v - mx) - lse;
+    store_val(p.out, p.out_dtype, base + c, v);
+  }
+}
+
+template <typename TH, int VEC, int LPG, int NV>
+struct Agg {
+  static constexpr int G = 32 / LPG;  // edge groups per warp
+  static constexpr int U = NV == 1 ? 4 : (NV == 2 ? 2 : 1);
+
+  // Accumulates edges [eb, ee) of `row`. Per-head running max / sum live in
+  // lane hd (m_reg, s_reg); acc is the group-partial weighted sum.
+  static __device__ __forceinline__ void range(const AggParams& p, int64_t row, int eb, int ee,
+                                               float (&acc)[NV][VEC], float& m_reg, float& s_reg,
+                                               int32_t* s_col, float* s_p, const int (&hv)[NV],
+                                               int lane) {
+    const int lig = lane % LPG;
+    const int grp = lane / LPG;
+    const char* hbase = reinterpret_cast<const char*>(p.h);
+    const size_t ldh_b = size_t(p.ldh) * sizeof(TH);
+    int voff[NV];
+    bool vok[NV];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const int e0 = (v * LPG + lig) * VEC;
+      voff[v] = e0 * int(sizeof(TH));
+      vok[v] = e0 < p.F;
+    }
+    float sc_reg = 1.f;
+    for (int cb = eb; cb < ee; cb += 32) {
+      const int k = cb + lane;
+      bool valid = k < ee;
+      int src = valid ? __ldg(p.col + k) : 0;
+      if (valid && unsigned(src) >= unsigned(p.n_src)) {
+        atomicOr(p.counters + 2, 1);
+        valid = false;
+        src = 0;
+      }
+      s_col[lane] = src;
+      if (p.mode == MODE_GCN) {
+        s_p[lane] = valid ? __ldg(p.w + k) : 0.f;
+      } else {
+        bool rescale = false;
+        for (int hd = 0; hd < p.H; ++hd) {
+          float e = -INFINITY;
+          if (valid) {
+            if (p.mode == MODE_GAT) {
+              const float x = __ldg(p.asrc + size_t(src) * p.H + hd) +
+                              __ldg(p.adst + size_t(row) * p.H + hd);
+              e = x > 0.f ? x : x * p.slope;
+            } else {
+              e = __ldg(p.scores + size_t(k) * p.H + hd);
+            }
+          }
+          const float cmax = warp_max(e);
+          const float m_old = __shfl_sync(kFull, m_reg, hd);
+          const float m_new = fmaxf(m_old, cmax);
+          const float pr = valid ? expf(e - m_new) : 0.f;
+          const float ps = warp_sum(pr);
+          const float sc = expf(m_old - m_new);  // 0 on the first chunk (m_old = -inf)
+          if (lane == hd) {
+            s_reg = s_reg * sc + ps;
+            m_reg = m_new;
+            sc_reg = sc;
+          }
+          rescale |= (cb != eb) && (m_new != m_old);
+          s_p[lane * p.HS + hd] = pr;
+        }
+        if (rescale) {
+#pragma unroll
+          for (int v = 0; v < NV; ++v) {
+            const float sc = __shfl_sync(kFull, sc_reg, hv[v]);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) acc[v][e] *= sc;
+          }
+        }
+      }
+      __syncwarp();
+      const int n = min(32, ee - cb);
+      int j = grp;
+      for (; j + (U - 1) * G < n; j += U * G) {
+        float hvv[U][NV][VEC];
+        const char* rows[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) rows[u] = hbase + size_t(s_col[j + u * G]) * ldh_b;
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+          for (int v = 0; v < NV; ++v) {
+            if (vok[v]) {
+              VecLoad<TH, VEC>::run(rows[u] + voff[v], hvv[u][v]);
+            } else {
+#pragma unroll
+              for (int e = 0; e < VEC; ++e) hvv[u][v][e] = 0.f;
+            }
+          }
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+          for (int v = 0; v < NV; ++v) {
+            const float a = s_p[(j + u * G) * p.HS + hv[v]];
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) acc[v][e] = fmaf(a, hvv[u][v][e], acc[v][e]);
+          }
+      }
+      for (; j < n; j += G) {
+        const char* r = hbase + size_t(s_col[j]) * ldh_b;
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+          if (!vok[v]) continue;
+          float x[VEC];
+          VecLoad<TH, VEC>::run(r + voff[v], x);
+          const float a = s_p[j * p.HS + hv[v]];
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) acc[v][e] = fmaf(a, x[e], acc[v][e]);
+        }
+      }
+      __syncwarp();
+    }
+  }
+
+  static __device__ __forceinline__ void group_reduce(float (&acc)[NV][VEC]) {
+#pragma unroll
+    for (int o = LPG; o < 32; o <<= 1)
+#pragma unroll
+      for (int v = 0; v < NV; ++v)
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) acc[v][e] += __shfl_xor_sync(kFull, acc[v][e], o);
+  }
+
+  // Writes the group-0 lanes' features (divided by den per head) into s_row.
+  static __device__ __forceinline__ void spill(const AggParams& p, const float (&acc)[NV][VEC],
+                                               float* s_row, const int (&hv)[NV], float den_reg,
+                                               bool divide, int lane) {
+    float den[NV];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) den[v] = __shfl_sync(kFull, den_reg, hv[v]);
+    if (lane < LPG) {
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        const int e0 = (v * LPG + lane) * VEC;
+#pragma unroll
+        for (int e = 0; e < VEC; ++e)
+          if (e0 + e < p.F) s_row[e0 + e] = divide ? acc[v][e] / den[v] : acc[v][e];
+      }
+    }
+  }
+};
+
+template <typename TH, int VEC, int LPG, int NV>
+__global__ void __launch_bounds__(kThreads) agg_kernel(const AggParams p) {
+  using A = Agg<TH, VEC, LPG, NV>;
+  extern __shared__ float smem[];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  // Shared memory carve-up (floats).
+  int32_t* s_col_all = reinterpret_cast<int32_t*>(smem);            // kWarps*32
+  float* s_p_all = smem + kWarps * 32;                                // kWarps*32*HS
+  float* s_row_all = s_p_all + kWarps * 32 * p.HS;                   // kWarps*F_pad
+  float* s_wm = s_row_all + kWarps * p.F_pad;                         // kWarps*kHMax
+  float* s_ws = s_wm + kWarps * kHMax;                                // kWarps*kHMax
+  float* s_fin = s_ws + kWarps * kHMax;                               // F_pad
+  float* s_hm = s_fin + p.F_pad;                                      // kHMax
+  float* s_hs = s_hm + kHMax;                                         // kHMax
+  __shared__ int s_item;
+
+  int32_t* s_col = s_col_all + warp * 32;
+  float* s_p = s_p_all + warp * 32 * p.HS;
+  float* s_row = s_row_all + warp * p.F_pad;
+  const bool softmax = p.mode != MODE_GCN;
+
+  int hv[NV];
+  {
+    const int lig = lane % LPG;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const int e0 = (v * LPG + lig) * VEC;
+      hv[v] = softmax ? min(e0 / p.C, p.H - 1) : 0;
+    }
+  }
+
+  // ---- Phase 1: CTA items (long rows and segments of split rows) ----
+  for (;;) {
+    if (threadIdx.x == 0) s_item = atomicAdd(p.counters + 0, 1);
+    __syncthreads();
+    const int it = s_item;
+    if (it >= p.n_cta_items) break;
+    const int4 item = p.cta_items[it];
+    const int64_t row = item.x;
+    const int eb = int(max(int64_t(item.y), p.e_lo)), ee = int(min(int64_t(item.z), p.e_hi));
+    const int slot = item.w;
+    const int len = ee - eb;
+    const int sub = ((len + kWarps - 1) / kWarps + 31) & ~31;
+    const int wb = min(ee, eb + warp * sub), we = min(ee, wb + sub);
+    float acc[NV][VEC];
+#pragma unroll
+    for (int v = 0; v < NV; ++v)
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc[v][e] = 0.f;
+    float m_reg = -INFINITY, s_reg = 0.f;
+    A::range(p, row, wb, we, acc, m_reg, s_reg, s_col, s_p, hv, lane);
+    A::group_reduce(acc);
+    A::spill(p, acc, s_row, hv, 1.f, false, lane);
+    if (lane < kHMax) {
+      s_wm[warp * kHMax + lane] = m_reg;
+      s_ws[warp * kHMax + lane] = s_reg;
+    }
+    __syncthreads();
+    if (softmax && threadIdx.x < p.H) {
+      const int hd = threadIdx.x;
+      float M = -INFINITY;
+      for (int w = 0; w < kWarps; ++w) M = fmaxf(M, s_wm[w * kHMax + hd]);
+      float S = 0.f;
+      for (int w = 0; w < kWarps; ++w) S += s_ws[w * kHMax + hd] * expf(s_wm[w * kHMax + hd] - M);
+      s_hm[hd] = M;
+      s_hs[hd] = S;
+    }
+    __syncthreads();
+    float* dst = slot >= 0 ? p.partials + size_t(slot) * p.part_stride : nullptr;
+    for (int c = threadIdx.x; c < p.F; c += kThreads) {
+      float a = 0.f;
+      if (softmax) {
+        const int hd = c / p.C;
+        const float M = s_hm[hd];
+        for (int w = 0; w < kWarps; ++w)
+          a += s_row_all[w * p.F_pad + c] * expf(s_wm[w * kHMax + hd] - M);
+      } else {
+        for (int w = 0; w < kWarps; ++w) a += s_row_all[w * p.F_pad + c];
+      }
+      if (dst) {
+        dst[2 * kHMax + c] = a;
+      } else {
+        s_fin[c] = softmax ? a / (s_hs[c / p.C] + p.eps) : a;
+      }
+    }
+    if (dst && threadIdx.x < kHMax) {
+      dst[threadIdx.x] = softmax ? s_hm[threadIdx.x] : 0.f;
+      dst[kHMax + threadIdx.x] = softmax ? s_hs[threadIdx.x] : 0.f;
+    }
+    __syncthreads();
+    if (!dst && warp == 0) warp_epilogue(p, row, s_fin, lane);
+    __syncthreads();
+  }
+
+  // ---- Phase 2: one warp per short row, edge-balanced row ranges ----
+  for (;;) {
+    int t = 0;
+    if (lane == 0) t = atomicAdd(p.counters + 1, 1);
+    t = __shfl_sync(kFull, t, 0);
+    if (t >= p.n_warp_tasks) break;
+    const int r0 = p.warp_tasks[t], r1 = p.warp_tasks[t + 1];
+    for (int r = r0; r < r1; ++r) {
+      const int eb = max(int64_t(__ldg(p.rowptr + r)), p.e_lo);
+      const int ee = min(int64_t(__ldg(p.rowptr + r + 1)), p.e_hi);
+      if (ee - eb > p.cta_threshold) continue;
+      float acc[NV][VEC];
+#pragma unroll
+      for (int v = 0; v < NV; ++v)
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) acc[v][e] = 0.f;
+      float m_reg = -INFINITY, s_reg = 0.f;
+      if (ee > eb) {
+        A::range(p, r, eb, ee, acc, m_reg, s_reg, s_col, s_p, hv, lane);
+        A::group_reduce(acc);
+      }
+      A::spill(p, acc, s_row, hv, s_reg + p.eps, softmax && ee > eb, lane);
+      __syncwarp();
+      warp_epilogue(p, r, s_row, lane);
+      __syncwarp();
+    }
+  }
+}
+
+// Combines the partial (max, sum, acc) slots of every split row in slot order.
+__global__ void __launch_bounds__(kThreads) merge_kernel(const AggParams p) {
+  extern __shared__ float smem[];
+  float* s_fin = smem;               // F_pad
+  float* s_hm = s_fin + p.F_pad;     // kHMax
+  float* s_hs = s_hm + kHMax;        // kHMax
+  const int4 sr = p.split_rows[blockIdx.x];
+  const int64_t row = sr.x;
+  const int first = sr.y, ns = sr.z;
+  const bool softmax = p.mode != MODE_GCN;
+  if (softmax && threadIdx.x < p.H) {
+    const int hd = threadIdx.x;
+    float M = -INFINITY;
+    for (int s = 0; s < ns; ++s) M = fmaxf(M, p.partials[size_t(first + s) * p.part_stride + hd]);
+    float S = 0.f;
+    for (int s = 0; s < ns; ++s) {
+      const float* q = p.partials + size_t(first + s) * p.part_stride;
+      S += q[kHMax + hd] * expf(q[hd] - M);
+    }
+    s_hm[hd] = M;
+    s_hs[hd] = S;
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < p.F; c += kThreads) {
+    float a = 0.f;
+    if (softmax) {
+      const int hd = c / p.C;
+      for (int s = 0; s < ns; ++s) {
+        const float* q = p.partials + size_t(first + s) * p.part_stride;
+        a += q[2 * kHMax + c] * expf(q[hd] - s_hm[hd]);
+      }
+      a = a / (s_hs[hd] + p.eps);
+    } else {
+      for (int s = 0; s < ns; ++s) a += p.partials[size_t(first + s) * p.part_stride + 2 * kHMax + c];
+    }
+    s_fin[c] = a;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) warp_epilogue(p, row, s_fin, threadIdx.x);
+}
+
+using KernelFn = void (*)(const AggParams);
+
+template <typename TH, int VEC>
+KernelFn pick_layout(int lpg, int nv) {
+  if (nv == 1) {
+    switch (lpg) {
+      case 1: return agg_kernel<TH, VEC, 1, 1>;
+      case 2: return agg_kernel<TH, VEC, 2, 1>;
+      case 4: return agg_kernel<TH, VEC, 4, 1>;
+      case 8: return agg_kernel<TH, VEC, 8, 1>;
+      case 16: return agg_kernel<TH, VEC, 16, 1>;
+      case 32: return agg_kernel<TH, VEC, 32, 1>;
+    }
+  } else if (lpg == 32) {
+    switch (nv) {
+      case 2: return agg_kernel<TH, VEC, 32, 2>;
+      case 4: return agg_kernel<TH, VEC, 32, 4>;
+      case 8: return agg_kernel<TH, VEC, 32, 8>;
+    }
+  }
+  return nullptr;
+}
+
+size_t agg_smem_bytes(int F_pad, int HS) {
+  return sizeof(float) * (size_t(kWarps) * 32 + size_t(kWarps) * 32 * HS +
+                          size_t(kWarps) * F_pad + 2 * kWarps * kHMax + F_pad + 2 * kHMax);
+}
+
+int part_stride_floats(int F) { return int(gnnc::align_up(size_t(2 * kHMax + F), 4)); }
+
+// Lanes per edge group and vectors per lane for feature width F at vector width vec.
+void row_layout(int F, int vec, int* lpg_out, int* nv_out) {
+  const int lanes = (F + vec - 1) / vec;
+  int lpg = 1;
+  while (lpg < lanes && lpg < 32) lpg <<= 1;
+  int nv = (lanes + 31) / 32;
+  if (nv > 1) nv = nv <= 2 ? 2 : (nv <= 4 ? 4 : (nv <= 8 ? 8 : 16));
+  *lpg_out = lpg;
+  *nv_out = nv;
+}
+
+int padded_width(int F, int vec) {
+  int lpg, nv;
+  row_layout(F, vec, &lpg, &nv);
+  return int(gnnc::align_up(size_t(lpg * vec * nv), 4));
+}
+
+struct Launch {
+  const gnnc_plan_t* plan;
+  const void* h;
+  int h_dtype;
+  int64_t ldh;
+};
+
+int run_aggregate(gnnc_ctx_t* ctx, const Launch& L, AggParams p) {
+  const gnnc_plan_t* plan = L.plan;
+  // Vector width: 16-byte loads when the row stride, base pointer and (for
+  // multi-head softmax) the head width allow it; scalar loads otherwise.
+  const int vmax = L.h_dtype == GNNC_BF16 ? 8 : 4;
+  const bool heads_ok = (p.mode == MODE_GCN) || p.H == 1 || (p.C % vmax == 0);
+  const bool align_ok = (reinterpret_cast<uintptr_t>(L.h) % 16 == 0) && (L.ldh % vmax == 0);
+  const int vec = (heads_ok && align_ok) ? vmax : 1;
+  int lpg, nv;
+  row_layout(p.F, vec, &lpg, &nv);
+  if (nv > 8)
+    return gnnc::set_error(ctx, GNNC_ERR_UNSUPPORTED,
+                           "feature width %d too large for the row kernel (vector width %d)", p.F,
+                           vec);
+  KernelFn fn = nullptr;
+  if (L.h_dtype == GNNC_BF16)
+    fn = vec == 8 ? pick_layout<__nv_bfloat16, 8>(lpg, nv) : pick_layout<__nv_bfloat16, 1>(lpg, nv);
+  else
+    fn = vec == 4 ? pick_layout<float, 4>(lpg, nv) : pick_layout<float, 1>(lpg, nv);
+  if (!fn) return gnnc::set_error(ctx, GNNC_ERR_UNSUPPORTED, "no kernel for layout");
+
+  p.F_pad = int(gnnc::align_up(size_t(lpg * vec * nv), 4));
+  p.HS = p.mode == MODE_GCN ? 1 : p.H;
+  p.part_stride = part_stride_floats(p.F_pad);
+  p.cta_items = plan->cta_items;
+  p.n_cta_items = plan->n_cta_items;
+  p.split_rows = plan->split_rows;
+  p.warp_tasks = plan->warp_tasks;
+  p.n_warp_tasks = plan->n_warp_tasks;
+  p.cta_threshold = plan->cta_threshold;
+  p.counters = ctx->dev_words;
+  p.partials = nullptr;
+  if (plan->n_segments > 0) {
+    const size_t need = size_t(plan->n_segments) * p.part_stride * sizeof(float);
+    int st = gnnc::ensure_workspace(ctx, need);
+    if (st) return st;
+    p.partials = reinterpret_cast<float*>(ctx->ws);
+  }
+  const size_t smem = agg_smem_bytes(p.F_pad, p.HS);
+  if (smem > 48 * 1024)
+    GNNC_CUDA_TRY(ctx, cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            int(smem)));
+  int per_sm = 0;
+  GNNC_CUDA_TRY(ctx, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, smem));
+  if (per_sm < 1) per_sm = 1;
+  const int grid = ctx->num_sms * per_sm;
+  GNNC_CUDA_TRY(ctx, cudaMemsetAsync(ctx->dev_words, 0, 2 * sizeof(int), ctx->stream));
+  fn<<<grid, kThreads, smem, ctx->stream>>>(p);
+  GNNC_CUDA_TRY(ctx, cudaGetLastError());
+  if (plan->n_split_rows > 0) {
+    const size_t msmem = sizeof(float) * (p.F_pad + 2 * kHMax);
+    merge_kernel<<<unsigned(plan->n_split_rows), kThreads, msmem, ctx->stream>>>(p);
+    GNNC_CUDA_TRY(ctx, cudaGetLastError());
+  }
+  return GNNC_OK;
+}
+
+int check_common(gnnc_ctx_t* ctx, const gnnc_plan_t* plan, const int32_t* rowptr,
+                 const int32_t* col, const void* h, int h_dtype, int64_t ldh, int64_t n_rows,
+                 int64_t n_src, int64_t F, int act, void* out, int out_dtype, int64_t ldo,
+                 int64_t F_out) {
+  GNNC_CHECK_ARG(ctx, plan != nullptr, "plan is null");
+  GNNC_CHECK_ARG(ctx, plan->n_rows == n_rows, "plan was built for %lld rows, call has %lld",
+                 (long long)plan->n_rows, (long long)n_rows);
+  GNNC_CHECK_ARG(ctx, plan->device == ctx->device, "plan belongs to another device");
+  GNNC_CHECK_ARG(ctx, n_rows >= 0 && n_src >= 0 && F > 0, "bad sizes");
+  GNNC_CHECK_ARG(ctx, n_rows == 0 || (rowptr && out), "null rowptr/out");
+  GNNC_CHECK_ARG(ctx, h != nullptr || n_src == 0, "null h");
+  GNNC_CHECK_ARG(ctx, h_dtype == GNNC_F32 || h_dtype == GNNC_BF16, "bad h dtype");
+  GNNC_CHECK_ARG(ctx, out_dtype == GNNC_F32 || out_dtype == GNNC_BF16, "bad out dtype");
+  GNNC_CHECK_ARG(ctx, act >= GNNC_ACT_NONE && act <= GNNC_ACT_ELU, "bad activation");
+  GNNC_CHECK_ARG(ctx, ldh >= F, "ldh (%lld) < F (%lld)", (long long)ldh, (long long)F);
+  GNNC_CHECK_ARG(ctx, ldo >= F_out, "ldo (%lld) < F_out (%lld)", (long long)ldo,
+                 (long long)F_out);
+  GNNC_CHECK_ARG(ctx, n_src < (int64_t(1) << 31), "n_src exceeds int32 indexing");
+  (void)col;
+  return GNNC_OK;
+}
+
+AggParams base_params(const gnnc_plan_t* plan) {
+  AggParams p{};
+  p.e_lo = plan->e_begin;
+  p.e_hi = plan->e_end;
+  return p;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Plan
+// ---------------------------------------------------------------------------
+
+extern "C" int gnnc_plan_create(gnnc_ctx_t* ctx, const int32_t* rowptr, int64_t n_rows,
+                                int32_t cta_threshold, int32_t split_threshold,
+                                gnnc_plan_t** out_plan) {
+  if (!ctx || !out_plan) return GNNC_ERR_INVALID;
+  *out_plan = nullptr;
+  GNNC_CHECK_ARG(ctx, n_rows >= 0 && n_rows < (int64_t(1) << 31), "bad n_rows");
+  GNNC_CHECK_ARG(ctx, rowptr != nullptr, "null rowptr");
+  if (cta_threshold <= 0) cta_threshold = 256;
+  if (split_threshold <= 0) split_threshold = 4096;
+  GNNC_CHECK_ARG(ctx, split_threshold >= cta_threshold, "split_threshold < cta_threshold");
+  GNNC_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  std::vector<int32_t> rp(size_t(n_rows) + 1);
+  GNNC_CUDA_TRY(ctx, cudaMemcpyAsync(rp.data(), rowptr, rp.size() * sizeof(int32_t),
+                                     cudaMemcpyDeviceToHost, ctx->stream));
+  GNNC_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+  if (rp[0] < 0)
+    return gnnc::set_error(ctx, GNNC_ERR_BOUNDS, "rowptr[0] = %d is negative", rp[0]);
+  for (int64_t r = 0; r < n_rows; ++r)
+    if (rp[r + 1] < rp[r])
+      return gnnc::set_error(ctx, GNNC_ERR_BOUNDS, "rowptr decreases at row %lld",
+                             (long long)r);
+
+  std::vector<int4> items, splits;
+  std::vector<int32_t> tasks;
+  int64_t n_warp = 0, n_cta = 0, n_seg = 0;
+  int max_deg = 0;
+  // Warp tasks: contiguous row ranges of roughly equal cost (edges + a fixed
+  // per-row overhead); rows taken by the CTA path cost one unit.
+  const int64_t kTaskCost = 768, kRowCost = 6;
+  int64_t cost = 0;
+  tasks.push_back(0);
+  for (int64_t r = 0; r < n_rows; ++r) {
+    const int deg = rp[r + 1] - rp[r];
+    max_deg = std::max(max_deg, deg);
+    if (deg > split_threshold) {
+      const int ns = (deg + split_threshold - 1) / split_threshold;
+      splits.push_back(make_int4(int(r), int(n_seg), ns, 0));
+      for (int s = 0; s < ns; ++s) {
+        const int eb = rp[r] + s * split_threshold;
+        const int ee = std::min(rp[r + 1], eb + split_threshold);
+        items.push_back(make_int4(int(r), eb, ee, int(n_seg + s)));
+      }
+      n_seg += ns;
+      cost += 1;
+    } else if (deg > cta_threshold) {
+      items.push_back(make_int4(int(r), rp[r], rp[r + 1], -1));
+      ++n_cta;
+      cost += 1;
+    } else {
+      ++n_warp;
+      cost += deg + kRowCost;
+    }
+    if (cost >= kTaskCost) {
+      tasks.push_back(int32_t(r + 1));
+      cost = 0;
+    }
+  }
+  if (tasks.back() != n_rows) tasks.push_back(int32_t(n_rows));
+  // Largest CTA items first, so the long ones do not form the tail.
+  std::stable_sort(items.begin(), items.end(),
+                   [](const int4& a, const int4& b) { return (a.z - a.y) > (b.z - b.y); });
+
+  gnnc_plan_t* plan = new gnnc_plan_t();
+  plan->n_rows = n_rows;
+  plan->cta_threshold = cta_threshold;
+  plan->split_threshold = split_threshold;
+  plan->n_warp_rows = n_warp;
+  plan->n_cta_rows = n_cta;
+  plan->n_split_rows = int64_t(splits.size());
+  plan->n_segments = n_seg;
+  plan->n_cta_items = int64_t(items.size());
+  plan->n_warp_tasks = int64_t(tasks.size()) - 1;
+  plan->max_degree = max_deg;
+  plan->device = ctx->device;
+  plan->e_begin = rp[0];
+  plan->e_end = rp[size_t(n_rows)];
+  auto upload = [&](void** dst, const void* src, size_t bytes) -> cudaError_t {
+    if (bytes == 0) bytes = 16;
+    cudaError_t e = cudaMalloc(dst, bytes);
+    if (e != cudaSuccess) return e;
+    if (src) return cudaMemcpyAsync(*dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream);
+    return cudaSuccess;
+  };
+  cudaError_t e = upload(reinterpret_cast<void**>(&plan->cta_items),
+                         items.empty() ? nullptr : items.data(), items.size() * sizeof(int4));
+  if (e == cudaSuccess)
+    e = upload(reinterpret_cast<void**>(&plan->split_rows),
+               splits.empty() ? nullptr : splits.data(), splits.size() * sizeof(int4));
+  if (e == cudaSuccess)
+    e = upload(reinterpret_cast<void**>(&plan->warp_tasks), tasks.data(),
+               tasks.size() * sizeof(int32_t));
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) {
+    gnnc_plan_destroy(plan);
+    return gnnc::cuda_status(ctx, e, "plan upload");
+  }
+  *out_plan = plan;
+  return GNNC_OK;
+}
+
+extern "C" int gnnc_plan_destroy(gnnc_plan_t* plan) {
+  if (!plan) return GNNC_OK;
+  cudaSetDevice(plan->device);
+  if (plan->cta_items) cudaFree(plan->cta_items);
+  if (plan->split_rows) cudaFree(plan->split_rows);
+  if (plan->warp_tasks) cudaFree(plan->warp_tasks);
+  delete plan;
+  return GNNC_OK;
+}
+
+extern "C" int gnnc_plan_info(const gnnc_plan_t* plan, int64_t* info) {
+  if (!plan || !info) return GNNC_ERR_INVALID;
+  info[0] = plan->n_rows;
+  info[1] = plan->n_warp_rows;
+  info[2] = plan->n_cta_rows;
+  info[3] = plan->n_split_rows;
+  info[4] = plan->n_segments;
+  info[5] = plan->max_degree;
+  return GNNC_OK;
+}
+
+extern "C" int gnnc_workspace_query(gnnc_ctx_t* ctx, const gnnc_plan_t* plan, int64_t F,
+                                    size_t* bytes) {
+  if (!ctx || !plan || !bytes || F <= 0) return GNNC_ERR_INVALID;
+  const int F_pad = std::max(padded_width(int(F), 1), std::max(padded_width(int(F), 4),
+                                                                padded_width(int(F), 8)));
+  *bytes = size_t(plan->n_segments) * part_stride_floats(F_pad) * sizeof(float);
+  return GNNC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Aggregation entry points
+// ---------------------------------------------------------------------------
+
+extern "C" int gnnc_gcn_aggregate(gnnc_ctx_t* ctx, const gnnc_plan_t* plan,
+                                  const int32_t* rowptr, const int32_t* col, const float* w,
+                                  const void* h, int h_dtype, int64_t ldh, int64_t n_rows,
+                                  int64_t n_src, int64_t F, const float* bias, int act,
+                                  int log_softmax, void* out, int out_dtype, int64_t ldo) {
+  if (!ctx) return GNNC_ERR_INVALID;
+  int st = check_common(ctx, plan, rowptr, col, h, h_dtype, ldh, n_rows, n_src, F, act, out,
+                        out_dtype, ldo, F);
+  if (st) return st;
+  if (n_rows == 0) return GNNC_OK;
+  GNNC_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  AggParams p = base_params(plan);
+  p.rowptr = rowptr; p.col = col; p.w = w; p.h = h; p.ldh = ldh;
+  p.n_rows = n_rows; p.n_src = n_src;
+  p.H = 1; p.C = int(F); p.F = int(F); p.F_out = int(F);
+  p.mode = MODE_GCN; p.concat = 1; p.act = act; p.log_softmax = log_softmax;
+  p.bias = bias; p.out = out; p.out_dtype = out_dtype; p.ldo = ldo; p.eps = 0.f;
+  return run_aggregate(ctx, Launch{plan, h, h_dtype, ldh}, p);
+}
+
+static int gat_like(gnnc_ctx_t* ctx, const gnnc_plan_t* plan, int mode, const int32_t* rowptr,
+                    const int32_t* col, const float* scores, const void* h, int h_dtype,
+                    int64_t ldh, const float* asrc, const float* adst, int64_t n_rows,
+                    int64_t n_src, int64_t H, int64_t C, float slope, float eps, int concat,
+                    const float* bias, int act, int log_softmax, void* out, int out_dtype,
+                    int64_t ldo) {
+  if (!ctx) return GNNC_ERR_INVALID;
+  GNNC_CHECK_ARG(ctx, H >= 1 && C >= 1, "bad heads/channels");
+  if (H > kHMax)
+    return gnnc::set_error(ctx, GNNC_ERR_UNSUPPORTED, "at most %d heads supported", kHMax);
+  const int64_t F = H * C, F_out = concat ? F : C;
+  int st = check_common(ctx, plan, rowptr, col, h, h_dtype, ldh, n_rows, n_src, F, act, out,
+                        out_dtype, ldo, F_out);
+  if (st) return st;
+  if (n_rows == 0) return GNNC_OK;
+  GNNC_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  AggParams p = base_params(plan);
+  p.rowptr = rowptr; p.col = col; p.scores = scores; p.asrc = asrc; p.adst = adst;
+  p.h = h; p.ldh = ldh; p.n_rows = n_rows; p.n_src = n_src;
+  p.H = int(H); p.C = int(C); p.F = int(F); p.F_out = int(F_out);
+  p.mode = mode; p.concat = concat; p.act = act; p.log_softmax = log_softmax;
+  p.slope = slope; p.eps = eps; p.bias = bias; p.out = out; p.out_dtype = out_dtype; p.ldo = ldo;
+  return run_aggregate(ctx, Launch{plan, h, h_dtype, ldh}, p);
+}
+
+extern "C" int gnnc_gat_aggregate(gnnc_ctx_t* ctx, const gnnc_plan_t* plan,
+                                  const int32_t* rowptr, const int32_t* col, const void* h,
+                                  int h_dtype, int64_t ldh, const float* asrc, const float* adst,
+                                  int64_t n_rows, int64_t n_src, int64_t H, int64_t C,
+                                  float negative_slope, int concat, const float* bias, int act,
+                                  int log_softmax, void* out, int out_dtype, int64_t ldo) {
+  if (ctx && n_rows > 0 && (!asrc || !adst))
+    return gnnc::set_error(ctx, GNNC_ERR_INVALID, "null attention coefficients");
+  return gat_like(ctx, plan, MODE_GAT, rowptr, col, nullptr, h, h_dtype, ldh, asrc, adst, n_rows,
+                  n_src, H, C, negative_slope, 1e-16f, concat, bias, act, log_softmax, out,
+                  out_dtype, ldo);
+}
+
+extern "C" int gnnc_softmax_aggregate(gnnc_ctx_t* ctx, const gnnc_plan_t* plan,
+                                      const int32_t* rowptr, const int32_t* col, const float* s,
+                                      const void* h, int h_dtype, int64_t ldh, int64_t n_rows,
+                                      int64_t n_src, int64_t H, int64_t C, float eps, int concat,
+                                      const float* bias, int act, int log_softmax, void* out,
+                                      int out_dtype, int64_t ldo) {
+  if (ctx && n_rows > 0 && !s) return gnnc::set_error(ctx, GNNC_ERR_INVALID, "null scores");
+  return gat_like(ctx, plan, MODE_SCORES, rowptr, col, s, h, h_dtype, ldh, nullptr, nullptr,
+                  n_rows, n_src, H, C, 0.f, eps, concat, bias, act, log_softmax, out, out_dtype,
+                  ldo);
+}

@@ -1,0 +1,400 @@
+"""B200 lowering: torch model -> kernel program -> executable.
+
+The reference lowers a PyG model through torch.export, torch-mlir and the MLIR
+sparsifier (gnnc/compile.py:109-124, gnnc/schedule/sparse.py:21-114); its
+aggregation reaches the backend as aten._sparse_mm (test/reference/gcn.raw.mlir:7).
+The B200 target instead traces the model with torch.fx, keeping GCNConv /
+GATConv modules as leaves, and matches the chain
+
+    x -> conv -> [relu | elu] -> [dropout(eval)] -> conv -> ... -> [log_softmax]
+
+into one LayerOp per conv. Each LayerOp becomes two kernel launches: the dense
+projection (gnnc_proj, with GAT's attention coefficients in its epilogue) and
+the aggregation (gnnc_gcn_aggregate / gnnc_gat_aggregate) with bias, the
+activation and the final log_softmax fused into its epilogue.
+"""
+
+from __future__ import annotations
+
+import operator
+from dataclasses import dataclass, field
+
+import torch
+import torch.fx as fx
+import torch.nn.functional as F
+
+from gnnc.b200 import runtime as rt
+
+_CONV_CLASSES = ("GCNConv", "GATConv")
+
+
+def _is_conv(mod: torch.nn.Module) -> bool:
+    return type(mod).__name__ in _CONV_CLASSES
+
+
+class _Tracer(fx.Tracer):
+    def is_leaf_module(self, m: torch.nn.Module, qualname: str) -> bool:
+        return _is_conv(m) or super().is_leaf_module(m, qualname)
+
+
+def trace(model: torch.nn.Module) -> fx.GraphModule:
+    """fx graph of `model` with GCNConv / GATConv kept as call_module leaves."""
+    model.eval()
+    graph = _Tracer().trace(model)
+    return fx.GraphModule(model, graph)
+
+
+@dataclass
+class LayerOp:
+    name: str
+    kind: str  # "gcn" | "gat"
+    in_channels: int
+    heads: int
+    channels: int  # per head
+    concat: bool
+    negative_slope: float
+    normalize: bool
+    add_self_loops: bool
+    weight: torch.Tensor  # [heads*channels, in]
+    att_src: torch.Tensor | None
+    att_dst: torch.Tensor | None
+    bias: torch.Tensor | None
+    act: int = rt.ACT_NONE
+    log_softmax: bool = False
+
+    @property
+    def width(self) -> int:
+        return self.heads * self.channels
+
+    @property
+    def out_width(self) -> int:
+        return self.width if self.concat else self.channels
+
+    def describe(self) -> str:
+        act = {rt.ACT_NONE: "none", rt.ACT_RELU: "relu", rt.ACT_ELU: "elu"}[self.act]
+        proj = f"gnnc_proj [{self.in_channels} -> {self.width}]"
+        if self.kind == "gat":
+            proj += f" + attention coefficients (heads={self.heads})"
+            agg = (
+                f"gnnc_gat_aggregate heads={self.heads} C={self.channels} "
+                f"slope={self.negative_slope} concat={int(self.concat)}"
+            )
+        else:
+            agg = f"gnnc_gcn_aggregate F={self.width} normalize={int(self.normalize)}"
+        epi = f"bias={'yes' if self.bias is not None else 'no'} act={act}"
+        epi += " log_softmax" if self.log_softmax else ""
+        return f"  {self.name}: {proj}\n  {self.name}: {agg} epilogue({epi})"
+
+
+@dataclass
+class B200Program:
+    layers: list[LayerOp]
+    input_names: list[str]
+    feature_dtype: torch.dtype = torch.float32
+    notes: list[str] = field(default_factory=list)
+
+    def __str__(self) -> str:
+        lines = [f"b200.program(inputs={self.input_names}, features={self.feature_dtype})"]
+        lines += [layer.describe() for layer in self.layers]
+        return "\n".join(lines)
+
+
+def _layer_from_module(name: str, mod: torch.nn.Module) -> LayerOp:
+    cls = type(mod).__name__
+    if cls == "GCNConv":
+        if getattr(mod, "improved", False):
+            raise NotImplementedError(f"{name}: GCNConv(improved=True) is not supported")
+        lin = mod.lin
+        w = lin.weight.detach()
+        return LayerOp(
+            name=name, kind="gcn", in_channels=w.size(1), heads=1, channels=w.size(0),
+            concat=True, negative_slope=0.0, normalize=bool(getattr(mod, "normalize", True)),
+            add_self_loops=bool(getattr(mod, "add_self_loops", True)), weight=w,
+            att_src=None, att_dst=None,
+            bias=None if mod.bias is None else mod.bias.detach(),
+        )
+    # GATConv: PyG >= 2.5 names the shared projection `lin`; older releases `lin_src`.
+    lin = getattr(mod, "lin", None)
+    if lin is None:
+        lin = mod.lin_src
+        if getattr(mod, "lin_dst", lin) is not lin:
+            raise NotImplementedError(f"{name}: bipartite GATConv is not supported")
+    if getattr(mod, "edge_dim", None) is not None or getattr(mod, "residual", False):
+        raise NotImplementedError(f"{name}: edge features / residual GATConv not supported")
+    H, C = int(mod.heads), int(mod.out_channels)
+    w = lin.weight.detach()
+    return LayerOp(
+        name=name, kind="gat", in_channels=w.size(1), heads=H, channels=C,
+        concat=bool(mod.concat), negative_slope=float(mod.negative_slope), normalize=False,
+        add_self_loops=bool(mod.add_self_loops), weight=w,
+        att_src=mod.att_src.detach().reshape(-1), att_dst=mod.att_dst.detach().reshape(-1),
+        bias=None if mod.bias is None else mod.bias.detach(),
+    )
+
+
+_RELU = {F.relu, torch.relu, torch.nn.functional.relu}
+_ELU = {F.elu, torch.nn.functional.elu}
+_LOGSM = {F.log_softmax, torch.log_softmax}
+_DROPOUT = {F.dropout, torch.nn.functional.dropout}
+
+
+def lower_graph(gm: fx.GraphModule, feature_dtype: torch.dtype | None = None) -> B200Program:
+    """Matches the conv / activation chain of `gm` into a B200Program."""
+    modules = dict(gm.named_modules())
+    placeholders: list[str] = []
+    value: dict[fx.Node, str] = {}
+    layers: list[LayerOp] = []
+    graph_arg: fx.Node | None = None
+    current: fx.Node | None = None
+
+    def expect_current(node: fx.Node, arg) -> None:
+        if arg is not current:
+            raise NotImplementedError(
+                f"{node.format_node()}: only a linear chain of GCNConv/GATConv layers is supported"
+            )
+
+    def act_of(node: fx.Node) -> int | None:
+        if node.op == "call_function" and node.target in _RELU:
+            return rt.ACT_RELU
+        if node.op == "call_method" and node.target == "relu":
+            return rt.ACT_RELU
+        if node.op == "call_module" and isinstance(modules[node.target], torch.nn.ReLU):
+            return rt.ACT_RELU
+        if node.op == "call_function" and node.target in _ELU:
+            alpha = node.kwargs.get("alpha", node.args[1] if len(node.args) > 1 else 1.0)
+            if alpha != 1.0:
+                raise NotImplementedError("elu with alpha != 1")
+            return rt.ACT_ELU
+        if node.op == "call_module" and isinstance(modules[node.target], torch.nn.ELU):
+            if modules[node.target].alpha != 1.0:
+                raise NotImplementedError("elu with alpha != 1")
+            return rt.ACT_ELU
+        return None
+
+    for node in gm.graph.nodes:
+        if node.op == "placeholder":
+            placeholders.append(node.target)
+            if len(placeholders) == 1:
+                current = node
+            elif len(placeholders) == 2:
+                graph_arg = node
+            else:
+                raise NotImplementedError("models take (x, adjacency or edge_index)")
+            continue
+        if node.op == "call_module" and _is_conv(modules[node.target]):
+            expect_current(node, node.args[0])
+            if len(node.args) < 2 or node.args[1] is not graph_arg or len(node.args) > 2 or node.kwargs:
+                raise NotImplementedError(f"{node.target}: call it as conv(x, graph)")
+            layers.append(_layer_from_module(node.target, modules[node.target]))
+            current = node
+            continue
+        act = act_of(node)
+        if act is not None:
+            expect_current(node, node.args[0])
+            if not layers or layers[-1].act != rt.ACT_NONE or layers[-1].log_softmax:
+                raise NotImplementedError(f"{node.format_node()}: activation must follow a conv")
+            layers[-1].act = act
+            current = node
+            continue
+        if (node.op == "call_function" and node.target in _DROPOUT) or (
+            node.op == "call_module" and isinstance(modules[node.target], torch.nn.Dropout)
+        ):
+            expect_current(node, node.args[0])
+            training = node.kwargs.get("training", node.args[2] if len(node.args) > 2 else True)
+            if node.op == "call_module":
+                training = modules[node.target].training
+            if training:
+                raise NotImplementedError("dropout in training mode")
+            current = node
+            continue
+        is_lsm = (node.op == "call_function" and node.target in _LOGSM) or (
+            node.op == "call_method" and node.target == "log_softmax"
+        )
+        if is_lsm:
+            expect_current(node, node.args[0])
+            dim = node.kwargs.get("dim", node.args[1] if len(node.args) > 1 else None)
+            if dim not in (-1, 1) or not layers:
+                raise NotImplementedError("log_softmax must be over the feature dim after a conv")
+            layers[-1].log_softmax = True
+            current = node
+            continue
+        if node.op == "output":
+            out = node.args[0]
+            if isinstance(out, (tuple, list)):
+                if len(out) != 1:
+                    raise NotImplementedError("multi-output models are not supported")
+                out = out[0]
+            expect_current(node, out)
+            continue
+        if node.op == "call_function" and node.target is operator.getitem:
+            raise NotImplementedError(f"{node.format_node()}: unsupported indexing")
+        raise NotImplementedError(f"op {node.format_node()} is not supported by the b200 target")
+
+    if not layers:
+        raise NotImplementedError("no GCNConv/GATConv layer found")
+    for prev, nxt in zip(layers, layers[1:], strict=False):
+        if prev.out_width != nxt.in_channels:
+            raise ValueError(f"{nxt.name} expects {nxt.in_channels} features, gets {prev.out_width}")
+    return B200Program(layers=layers, input_names=placeholders,
+                       feature_dtype=feature_dtype or torch.float32)
+
+
+# ---------------------------------------------------------------------------
+# Execution
+# ---------------------------------------------------------------------------
+
+
+@dataclass
+class DeviceGraph:
+    """A graph resident on one device in the layout the kernels read."""
+
+    rowptr: torch.Tensor  # int32 [N+1]
+    col: torch.Tensor  # int32 [E]
+    w: torch.Tensor | None  # fp32 [E] (GCN weights) or None (GAT)
+    plan: rt.Plan
+    num_nodes: int
+
+    @property
+    def num_edges(self) -> int:
+        return self.col.numel()
+
+
+def graph_from_csr(adj: torch.Tensor, device, *, cta_threshold=0, split_threshold=0) -> DeviceGraph:
+    """Pre-normalised torch.sparse_csr adjacency -> DeviceGraph (values kept as weights).
+
+    Follows the (crow_indices, col_indices, values) decomposition of
+    gnnc/execution/__init__.py:72-100; indices are narrowed to int32."""
+    crow = adj.crow_indices()
+    col = adj.col_indices()
+    if adj.size(0) != adj.size(1):
+        raise ValueError("adjacency must be square")
+    if col.numel() >= 2**31:
+        raise ValueError("more than 2^31 edges")
+    rowptr = crow.to(device=device, dtype=torch.int32, non_blocking=True).contiguous()
+    col = col.to(device=device, dtype=torch.int32, non_blocking=True).contiguous()
+    w = adj.values().to(device=device, dtype=torch.float32, non_blocking=True).contiguous()
+    rt.validate_csr(rowptr, col, adj.size(1))
+    plan = rt.Plan(rowptr, cta_threshold=cta_threshold, split_threshold=split_threshold)
+    return DeviceGraph(rowptr, col, w, plan, adj.size(0))
+
+
+def graph_from_edge_index(
+    edge_index: torch.Tensor,
+    num_nodes: int,
+    device,
+    *,
+    self_loops: bool,
+    dedupe: bool,
+    normalize: bool,
+    cta_threshold: int = 0,
+    split_threshold: int = 0,
+) -> DeviceGraph:
+    """edge_index [2,E] -> CSR by destination on the device (+ GCN weights)."""
+    ei = edge_index.to(device=device, dtype=torch.int64, non_blocking=True)
+    rowptr, col, mult = rt.csr_from_coo(ei, num_nodes, self_loops=self_loops, dedupe=dedupe)
+    w = None
+    if normalize:
+        _, _, w = rt.gcn_norm(rowptr, col, mult)
+    elif dedupe:
+        w = mult.to(torch.float32)
+    plan = rt.Plan(rowptr, cta_threshold=cta_threshold, split_threshold=split_threshold)
+    return DeviceGraph(rowptr, col, w, plan, num_nodes)
+
+
+def to_device_features(x: torch.Tensor, dtype: torch.dtype, device) -> torch.Tensor:
+    """Copies x into a row-padded (16-byte aligned rows) device buffer of `dtype`."""
+    out = rt.empty_rows(x.size(0), x.size(1), dtype, device)
+    out.copy_(x, non_blocking=True)
+    return out
+
+
+class B200Executable:
+    """A lowered model bound to one CUDA device. Call with the forward inputs."""
+
+    def __init__(self, program: B200Program, device: torch.device | str | None = None) -> None:
+        self.program = program
+        self.device = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device()
+        )
+        dt = program.feature_dtype
+        self._weights = []
+        for layer in program.layers:
+            w = layer.weight.to(device=self.device, dtype=dt)
+            w = to_device_features(w, dt, self.device)
+            asrc = adst = None
+            if layer.att_src is not None:
+                asrc = layer.att_src.to(self.device, torch.float32).contiguous()
+                adst = layer.att_dst.to(self.device, torch.float32).contiguous()
+            bias = None if layer.bias is None else layer.bias.to(self.device, torch.float32)
+            self._weights.append((w, asrc, adst, bias))
+        self._graphs: dict[tuple, tuple[object, DeviceGraph]] = {}
+
+    def __str__(self) -> str:
+        return f"b200.executable(device={self.device})\n{self.program}"
+
+    # Graphs are cached per (tensor identity, version, layer graph mode); the
+    # cache holds the source tensor so its id cannot be reused meanwhile.
+    def _graph_for(self, graph: torch.Tensor, num_nodes: int, layer: LayerOp) -> DeviceGraph:
+        if graph.layout == torch.sparse_csr:
+            if layer.kind != "gcn" or layer.normalize:
+                raise NotImplementedError(
+                    "a sparse CSR adjacency must be pre-normalised for GCNConv(normalize=False)"
+                )
+            mode = ("csr",)
+        elif graph.layout == torch.strided:
+            if layer.kind == "gcn":
+                mode = ("coo", layer.add_self_loops, True, layer.normalize)
+            else:
+                mode = ("coo", layer.add_self_loops, False, False)
+        else:
+            raise NotImplementedError(f"unsupported graph layout {graph.layout}")
+        key = (id(graph), graph._version, *mode)
+        hit = self._graphs.get(key)
+        if hit is not None and hit[0] is graph:
+            return hit[1]
+        if mode[0] == "csr":
+            g = graph_from_csr(graph, self.device)
+        else:
+            g = graph_from_edge_index(
+                graph, num_nodes, self.device, self_loops=mode[1], dedupe=mode[2], normalize=mode[3]
+            )
+        if len(self._graphs) > 4:
+            self._graphs.clear()
+        self._graphs[key] = (graph, g)
+        return g
+
+    def run_device(self, x: torch.Tensor, graph: torch.Tensor) -> torch.Tensor:
+        """Forward on device-resident (or host) inputs; returns the device output."""
+        dt = self.program.feature_dtype
+        n = x.size(0)
+        h_in = to_device_features(x, dt, self.device)
+        layers = self.program.layers
+        with torch.cuda.device(self.device):
+            for i, (layer, (w, asrc_w, adst_w, bias)) in enumerate(zip(layers, self._weights, strict=True)):
+                g = self._graph_for(graph, n, layer)
+                last = i == len(layers) - 1
+                out_dtype = torch.float32 if last else dt
+                if layer.kind == "gcn":
+                    h = rt.proj(h_in, w, out_dtype=dt)
+                    h_in = rt.gcn_aggregate(
+                        g.plan, g.rowptr, g.col, g.w, h, bias=bias, act=layer.act,
+                        log_softmax=layer.log_softmax, out_dtype=out_dtype,
+                    )
+                else:
+                    h, asrc, adst = rt.proj(h_in, w, att_src=asrc_w, att_dst=adst_w,
+                                            heads=layer.heads, out_dtype=dt)
+                    h_in = rt.gat_aggregate(
+                        g.plan, g.rowptr, g.col, h, asrc, adst, heads=layer.heads,
+                        negative_slope=layer.negative_slope, concat=layer.concat, bias=bias,
+                        act=layer.act, log_softmax=layer.log_softmax, out_dtype=out_dtype,
+                    )
+        return h_in
+
+    def __call__(self, *inputs: torch.Tensor) -> list[torch.Tensor]:
+        if len(inputs) != 2:
+            raise ValueError(f"expected (x, graph) inputs, got {len(inputs)}")
+        x, graph = inputs
+        out = self.run_device(x, graph)
+        if not x.is_cuda:
+            return [out.to("cpu")]
+        return [out.contiguous()]

@@ -1,0 +1,422 @@
+"""Python surface of the B200 runtime: contexts, plans and the hot-path ops.
+
+Every op takes and returns torch CUDA tensors (torch is the device-memory and
+stream plumbing here) and calls straight into libgnnc_b200.so through the C
+ABI; nothing in this module computes on the host. 2-D feature tensors may be
+row-padded views (stride(1) == 1, stride(0) >= width): the padding keeps every
+row 16-byte aligned so the kernels can use vector loads.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from gnnc.b200 import _lib
+from gnnc.b200._lib import ACT_ELU, ACT_NONE, ACT_RELU, BF16, F32, GnncError, raise_for
+
+__all__ = [
+    "ACT_ELU",
+    "ACT_NONE",
+    "ACT_RELU",
+    "Context",
+    "GnncError",
+    "Plan",
+    "csr_from_coo",
+    "empty_rows",
+    "gat_aggregate",
+    "gcn_aggregate",
+    "gcn_norm",
+    "proj",
+    "softmax_aggregate",
+    "validate_csr",
+]
+
+_DTYPES = {torch.float32: F32, torch.bfloat16: BF16}
+
+
+def _dt(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {t.dtype}; expected float32 or bfloat16") from None
+
+
+def _p(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _ld(t: torch.Tensor) -> int:
+    """Row stride of a 2-D feature tensor; its storage must cover every padded row."""
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError("feature tensors must be 2-D with unit column stride")
+    ld = t.stride(0) if t.size(0) > 1 else max(t.stride(0), t.size(1))
+    need = (t.storage_offset() + t.size(0) * ld) * t.element_size()
+    if t.numel() and t.untyped_storage().nbytes() < need:
+        raise ValueError("row-padded tensor whose storage does not cover the last row's padding")
+    return ld
+
+
+def _check_edges(plan: "Plan", *arrays: torch.Tensor | None) -> None:
+    for a in arrays:
+        if a is not None and a.size(0) < plan.num_edges:
+            raise ValueError(f"edge array has {a.size(0)} entries, the CSR needs {plan.num_edges}")
+
+
+def _check_cuda(*ts: torch.Tensor | None) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("B200 ops take CUDA tensors")
+
+
+def row_stride(width: int, dtype: torch.dtype) -> int:
+    """Row stride (elements) that keeps rows 16-byte aligned."""
+    per = 16 // torch.empty((), dtype=dtype).element_size()
+    return (width + per - 1) // per * per
+
+
+def empty_rows(n: int, width: int, dtype: torch.dtype, device) -> torch.Tensor:
+    """[n, width] view of an [n, row_stride(width)] buffer (16-byte aligned rows)."""
+    ld = row_stride(width, dtype)
+    buf = torch.empty((n, ld), dtype=dtype, device=device)
+    return buf[:, :width]
+
+
+class Context:
+    """One libgnnc_b200 context per CUDA device per process."""
+
+    _lock = threading.Lock()
+    _by_device: dict[int, Context] = {}
+
+    def __init__(self, device: int) -> None:
+        lib = _lib.load()
+        handle = ctypes.c_void_p()
+        st = lib.gnnc_init(device, ctypes.byref(handle))
+        if st != _lib.OK:
+            raise_for(st, None, f"gnnc_init(device={device})")
+        self.lib = lib
+        self.handle = handle.value
+        self.device = device
+
+    @classmethod
+    def get(cls, device: torch.device | int | None = None) -> Context:
+        if device is None:
+            idx = torch.cuda.current_device()
+        elif isinstance(device, int):
+            idx = device
+        else:
+            device = torch.device(device)
+            idx = device.index if device.index is not None else torch.cuda.current_device()
+        with cls._lock:
+            ctx = cls._by_device.get(idx)
+            if ctx is None:
+                ctx = cls._by_device[idx] = Context(idx)
+        return ctx
+
+    def use_current_stream(self) -> None:
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        self.lib.gnnc_stream_set(self.handle, stream)
+
+    def call(self, name: str, *args) -> None:
+        self.use_current_stream()
+        st = getattr(self.lib, name)(self.handle, *args)
+        raise_for(st, self.handle, name)
+
+    def synchronize(self) -> None:
+        raise_for(self.lib.gnnc_synchronize(self.handle), self.handle, "gnnc_synchronize")
+
+    def workspace_bind(self, buf: torch.Tensor | None) -> None:
+        ptr = None if buf is None else buf.data_ptr()
+        n = 0 if buf is None else buf.numel() * buf.element_size()
+        raise_for(self.lib.gnnc_workspace_bind(self.handle, ptr, n), self.handle, "workspace_bind")
+
+
+class Plan:
+    """Degree-skew row schedule of one CSR (gnnc_plan_create)."""
+
+    def __init__(
+        self,
+        rowptr: torch.Tensor,
+        *,
+        cta_threshold: int = 0,
+        split_threshold: int = 0,
+        ctx: Context | None = None,
+    ) -> None:
+        _check_cuda(rowptr)
+        if rowptr.dtype != torch.int32 or not rowptr.is_contiguous():
+            raise ValueError("rowptr must be a contiguous int32 CUDA tensor")
+        self.ctx = ctx or Context.get(rowptr.device)
+        self.n_rows = rowptr.numel() - 1
+        handle = ctypes.c_void_p()
+        self.ctx.use_current_stream()
+        st = self.ctx.lib.gnnc_plan_create(
+            self.ctx.handle,
+            rowptr.data_ptr(),
+            self.n_rows,
+            cta_threshold,
+            split_threshold,
+            ctypes.byref(handle),
+        )
+        raise_for(st, self.ctx.handle, "gnnc_plan_create")
+        self.handle = handle.value
+        # rowptr is host-validated by plan creation; keep its edge span for size checks
+        ends = rowptr[[0, -1]].tolist()
+        self.num_edges = int(ends[1])
+        self.first_edge = int(ends[0])
+
+    def info(self) -> dict[str, int]:
+        arr = (ctypes.c_int64 * 6)()
+        raise_for(self.ctx.lib.gnnc_plan_info(self.handle, arr), None, "gnnc_plan_info")
+        keys = ("n_rows", "n_warp_rows", "n_cta_rows", "n_split_rows", "n_segments", "max_degree")
+        return dict(zip(keys, list(arr), strict=True))
+
+    def workspace_bytes(self, width: int) -> int:
+        out = ctypes.c_size_t()
+        st = self.ctx.lib.gnnc_workspace_query(self.ctx.handle, self.handle, width, ctypes.byref(out))
+        raise_for(st, self.ctx.handle, "gnnc_workspace_query")
+        return out.value
+
+    def __del__(self) -> None:
+        h = getattr(self, "handle", None)
+        if h:
+            try:
+                self.ctx.lib.gnnc_plan_destroy(h)
+            except Exception:  # pragma: no cover - interpreter teardown
+                pass
+            self.handle = None
+
+
+# ---------------------------------------------------------------------------
+# Graph preparation
+# ---------------------------------------------------------------------------
+
+
+def csr_from_coo(
+    edge_index: torch.Tensor, num_nodes: int, *, self_loops: bool, dedupe: bool
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor | None]:
+    """COO edge_index [2,E] (int64, CUDA) -> CSR by destination.
+
+    Returns (rowptr int32 [N+1], col int32 [E'], mult int32 [E'] or None).
+    Column order within a row is ascending source id (torch coalesce order).
+    """
+    _check_cuda(edge_index)
+    if edge_index.dim() != 2 or edge_index.size(0) != 2:
+        raise ValueError("edge_index must be [2, E]")
+    ei = edge_index.to(torch.int64)
+    src = ei[0].contiguous()
+    dst = ei[1].contiguous()
+    E = src.numel()
+    cap = E + (num_nodes if self_loops else 0)
+    dev = edge_index.device
+    rowptr = torch.empty(num_nodes + 1, dtype=torch.int32, device=dev)
+    col = torch.empty(max(cap, 1), dtype=torch.int32, device=dev)
+    mult = torch.empty(max(cap, 1), dtype=torch.int32, device=dev) if dedupe else None
+    ctx = Context.get(dev)
+    e_out = ctypes.c_int64()
+    ctx.call(
+        "gnnc_csr_from_coo",
+        src.data_ptr(),
+        dst.data_ptr(),
+        E,
+        num_nodes,
+        int(self_loops),
+        int(dedupe),
+        rowptr.data_ptr(),
+        col.data_ptr(),
+        _p(mult),
+        cap,
+        ctypes.byref(e_out),
+    )
+    n = e_out.value
+    return rowptr, col[:n], (mult[:n] if mult is not None else None)
+
+
+def gcn_norm(
+    rowptr: torch.Tensor, col: torch.Tensor, mult: torch.Tensor | None = None
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """PyG gcn_norm weights on a CSR that already holds its self-loops.
+
+    Returns (deg fp32 [N], dinv fp32 [N], w fp32 [E])."""
+    _check_cuda(rowptr, col, mult)
+    N = rowptr.numel() - 1
+    dev = rowptr.device
+    deg = torch.empty(N, dtype=torch.float32, device=dev)
+    dinv = torch.empty(N, dtype=torch.float32, device=dev)
+    w = torch.empty(max(col.numel(), 1), dtype=torch.float32, device=dev)
+    Context.get(dev).call(
+        "gnnc_gcn_norm", rowptr.data_ptr(), col.data_ptr(), _p(mult), N, deg.data_ptr(),
+        dinv.data_ptr(), w.data_ptr(),
+    )
+    return deg, dinv, w[: col.numel()]
+
+
+def validate_csr(rowptr: torch.Tensor, col: torch.Tensor, n_src: int) -> None:
+    """Raises GnncInvalidArgument unless the CSR indexes [0, n_src) consistently."""
+    _check_cuda(rowptr, col)
+    Context.get(rowptr.device).call(
+        "gnnc_csr_validate", rowptr.data_ptr(), col.data_ptr(), rowptr.numel() - 1, col.numel(),
+        n_src,
+    )
+
+
+# ---------------------------------------------------------------------------
+# Projection
+# ---------------------------------------------------------------------------
+
+
+def proj(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    *,
+    att_src: torch.Tensor | None = None,
+    att_dst: torch.Tensor | None = None,
+    heads: int = 1,
+    out_dtype: torch.dtype | None = None,
+):
+    """h = x . weight^T (+ GAT attention coefficients).
+
+    x [N,K] (fp32 or bf16, padded rows allowed); weight [F,K] same dtype.
+    Returns h [N,F] (row-padded) or (h, asrc [N,H], adst [N,H]) when att_* given.
+    """
+    _check_cuda(x, weight, att_src, att_dst)
+    if x.dtype != weight.dtype:
+        raise ValueError("x and weight must share a dtype")
+    N, K = x.shape
+    F = weight.size(0)
+    if weight.size(1) != K:
+        raise ValueError(f"weight is {tuple(weight.shape)}, x has {K} columns")
+    out_dtype = out_dtype or x.dtype
+    h = empty_rows(N, F, out_dtype, x.device)
+    att = att_src is not None
+    asrc = adst = None
+    if att:
+        asrc = torch.empty((N, heads), dtype=torch.float32, device=x.device)
+        adst = torch.empty((N, heads), dtype=torch.float32, device=x.device)
+        att_src = att_src.reshape(-1).to(torch.float32).contiguous()
+        att_dst = att_dst.reshape(-1).to(torch.float32).contiguous()
+    Context.get(x.device).call(
+        "gnnc_proj",
+        x.data_ptr(), _dt(x), _ld(x), weight.data_ptr(), _ld(weight), N, K, F,
+        _p(att_src), _p(att_dst), heads, h.data_ptr(), _dt(h), _ld(h), _p(asrc), _p(adst),
+    )
+    return (h, asrc, adst) if att else h
+
+
+# ---------------------------------------------------------------------------
+# Aggregation
+# ---------------------------------------------------------------------------
+
+
+def _out(n: int, width: int, dtype: torch.dtype, device, out: torch.Tensor | None):
+    if out is None:
+        return empty_rows(n, width, dtype, device)
+    if tuple(out.shape) != (n, width) or out.dtype != dtype:
+        raise ValueError(f"out must be [{n},{width}] {dtype}")
+    return out
+
+
+def gcn_aggregate(
+    plan: Plan,
+    rowptr: torch.Tensor,
+    col: torch.Tensor,
+    w: torch.Tensor,
+    h: torch.Tensor,
+    *,
+    bias: torch.Tensor | None = None,
+    act: int = ACT_NONE,
+    log_softmax: bool = False,
+    out_dtype: torch.dtype = torch.float32,
+    out: torch.Tensor | None = None,
+    n_src: int | None = None,
+) -> torch.Tensor:
+    """out = A . h (+bias, act, log_softmax); A = CSR (rowptr, col, w)."""
+    _check_cuda(rowptr, col, w, h, bias)
+    n_rows = rowptr.numel() - 1
+    F = h.size(1)
+    out = _out(n_rows, F, out_dtype, h.device, out)
+    _check_edges(plan, col, w)
+    bias = None if bias is None else bias.to(torch.float32).contiguous()
+    plan.ctx.call(
+        "gnnc_gcn_aggregate",
+        plan.handle, rowptr.data_ptr(), col.data_ptr(), w.data_ptr(), h.data_ptr(), _dt(h),
+        _ld(h), n_rows, h.size(0) if n_src is None else n_src, F, _p(bias), act,
+        int(log_softmax), out.data_ptr(), _dt(out), _ld(out),
+    )
+    return out
+
+
+def gat_aggregate(
+    plan: Plan,
+    rowptr: torch.Tensor,
+    col: torch.Tensor,
+    h: torch.Tensor,
+    asrc: torch.Tensor,
+    adst: torch.Tensor,
+    *,
+    heads: int,
+    negative_slope: float = 0.2,
+    concat: bool = True,
+    bias: torch.Tensor | None = None,
+    act: int = ACT_NONE,
+    log_softmax: bool = False,
+    out_dtype: torch.dtype = torch.float32,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Fused GATConv aggregation (SDDMM, LeakyReLU, edge softmax, SpMM, epilogue)."""
+    _check_cuda(rowptr, col, h, asrc, adst, bias)
+    n_rows = rowptr.numel() - 1
+    F = h.size(1)
+    if F % heads:
+        raise ValueError("feature width not divisible by heads")
+    C = F // heads
+    width = F if concat else C
+    out = _out(n_rows, width, out_dtype, h.device, out)
+    _check_edges(plan, col)
+    if asrc.shape != (h.size(0), heads) or adst.shape != (n_rows, heads):
+        raise ValueError("asrc must be [n_src, heads] and adst [n_rows, heads]")
+    bias = None if bias is None else bias.to(torch.float32).contiguous()
+    plan.ctx.call(
+        "gnnc_gat_aggregate",
+        plan.handle, rowptr.data_ptr(), col.data_ptr(), h.data_ptr(), _dt(h), _ld(h),
+        asrc.contiguous().data_ptr(), adst.contiguous().data_ptr(), n_rows, h.size(0), heads, C,
+        float(negative_slope), int(concat), _p(bias), act, int(log_softmax), out.data_ptr(),
+        _dt(out), _ld(out),
+    )
+    return out
+
+
+def softmax_aggregate(
+    plan: Plan,
+    rowptr: torch.Tensor,
+    col: torch.Tensor,
+    scores: torch.Tensor,
+    h: torch.Tensor,
+    *,
+    heads: int = 1,
+    eps: float = 1e-16,
+    concat: bool = True,
+    bias: torch.Tensor | None = None,
+    act: int = ACT_NONE,
+    log_softmax: bool = False,
+    out_dtype: torch.dtype = torch.float32,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Edge softmax of given scores [E, heads] followed by the weighted SpMM."""
+    _check_cuda(rowptr, col, scores, h, bias)
+    n_rows = rowptr.numel() - 1
+    F = h.size(1)
+    C = F // heads
+    width = F if concat else C
+    out = _out(n_rows, width, out_dtype, h.device, out)
+    scores = scores.to(torch.float32).contiguous().view(-1, heads)
+    _check_edges(plan, col, scores)
+    bias = None if bias is None else bias.to(torch.float32).contiguous()
+    plan.ctx.call(
+        "gnnc_softmax_aggregate",
+        plan.handle, rowptr.data_ptr(), col.data_ptr(), scores.data_ptr(), h.data_ptr(), _dt(h),
+        _ld(h), n_rows, h.size(0), heads, C, float(eps), int(concat), _p(bias), act,
+        int(log_softmax), out.data_ptr(), _dt(out), _ld(out),
+    )
+    return out

@@ -1,0 +1,79 @@
+"""From user-land Python to a (model, forward_inputs) pair.
+
+`get_model_and_data(model_file, dataset)` keeps the reference's behaviour
+(gnnc/ingress.py:25-49): load the model file, take inputs from its own
+get_inputs()/get_init_inputs() or from a named dataset, seed 0, build the model.
+Named datasets are the reference's real ones ("cora", "ogbn-arxiv", loaded
+through PyG/OGB when installed) and the seeded synthetic workloads of
+gnnc.examples.synthetic ("c1" ... "c5"). The torch-mlir import
+(import_as_raw_ir) belongs to the MLIR targets and is not part of this build.
+"""
+
+from __future__ import annotations
+
+import importlib.util
+from pathlib import Path
+
+import torch
+
+_DEFAULT_HIDDEN = 64
+
+
+def _load_module(model_file: Path):
+    spec = importlib.util.spec_from_file_location("_gnnc_model", str(model_file))
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module
+
+
+def get_model_and_data(model_file: Path, dataset: str | None = None):
+    module = _load_module(Path(model_file))
+    if dataset is None:
+        forward_inputs = module.get_inputs()
+        init_inputs = module.get_init_inputs()
+        init_kwargs = {}
+    else:
+        forward_inputs, init_inputs, init_kwargs = _dataset_inputs(Path(model_file).stem, dataset)
+    torch.manual_seed(0)
+    return module.Model(*init_inputs, **init_kwargs), forward_inputs
+
+
+def synthetic_inputs(model_name: str, name: str):
+    """(forward_inputs, init_inputs, init_kwargs) of a synthetic workload."""
+    from gnnc.examples import synthetic as S
+    from gnnc.examples.util import normalized_csr_adj
+
+    key = name
+    if name == "c4":
+        key = f"c4-{model_name}"
+    if key not in S.CONFIGS:
+        raise ValueError(f"unknown dataset: {name}")
+    cfg = S.CONFIGS[key]
+    if cfg.model != model_name:
+        raise ValueError(f"workload {name} is defined for model {cfg.model!r}, not {model_name!r}")
+    ei = S.make_graph(cfg)
+    x = S.make_features(cfg)
+    if model_name == "gcn":
+        graph = normalized_csr_adj(ei, cfg.num_nodes)
+        return (x, graph), (cfg.in_channels, cfg.hidden, cfg.out_channels), {"num_layers": cfg.num_layers}
+    kw = {"heads": cfg.heads, "num_layers": cfg.num_layers}
+    return (x, ei), (cfg.in_channels, cfg.hidden, cfg.out_channels), kw
+
+
+def _dataset_inputs(model_name: str, dataset: str):
+    from gnnc.examples.util import normalized_csr_adj
+    from gnnc.paths import DATA_DIR
+
+    if dataset not in ("cora", "ogbn-arxiv"):
+        return synthetic_inputs(model_name, dataset)
+    if dataset == "cora":
+        from torch_geometric.datasets import Planetoid
+
+        ds = Planetoid(root=str(DATA_DIR / "planetoid"), name="Cora")
+    else:
+        from ogb.nodeproppred import PygNodePropPredDataset
+
+        ds = PygNodePropPredDataset(name="ogbn-arxiv", root=str(DATA_DIR / "ogb"))
+    data = ds[0]
+    graph = normalized_csr_adj(data.edge_index, data.num_nodes) if model_name == "gcn" else data.edge_index
+    return (data.x, graph), (ds.num_node_features, _DEFAULT_HIDDEN, ds.num_classes), {}

@@ -1,0 +1,122 @@
+"""gnnc-bench: compile a model, execute it, compare to torch eager (and time it).
+
+    python -m gnnc.tools.gnnc_bench --model gcn
+    python -m gnnc.tools.gnnc_bench --model gat --dataset c2
+    python -m gnnc.tools.gnnc_bench --model gat --dataset c3 --dtype bf16 --time
+
+Same flow and exit codes as the reference's gnnc/tools/gnnc_bench.py:29-85:
+0 = PASS, 1 = output mismatch, 2 = ValueError / NotImplementedError,
+3 = ImportError (missing library). Differences: the default --target is b200
+(the MLIR cpu/gpu targets are not part of this build and exit 3), --dataset
+also accepts the synthetic workloads c1..c5, the comparison tolerance follows
+the feature dtype (rtol 1e-3 / atol 1e-4 for fp32 as in the reference; 2e-2
+for bf16 features), and --time reports CUDA-event medians per forward.
+"""
+
+from __future__ import annotations
+
+import argparse
+import sys
+
+import numpy as np
+
+from gnnc import __version__, paths
+from gnnc.examples import MODELS_DIR, available
+
+
+def _time_forward(lowered, inputs, warmup: int, iters: int) -> dict:
+    import torch
+
+    x, graph = inputs
+    dev = lowered.device
+    xd = x.to(dev)
+    gd = graph.to(dev)
+    for _ in range(warmup):
+        lowered.run_device(xd, gd)
+    torch.cuda.synchronize(dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(iters)]
+    stops = [torch.cuda.Event(enable_timing=True) for _ in range(iters)]
+    for i in range(iters):
+        starts[i].record()
+        lowered.run_device(xd, gd)
+        stops[i].record()
+    torch.cuda.synchronize(dev)
+    ms = sorted(s.elapsed_time(e) for s, e in zip(starts, stops, strict=True))
+    return {"median_ms": ms[len(ms) // 2], "p90_ms": ms[int(len(ms) * 0.9)], "iters": iters}
+
+
+def main(argv: list[str] | None = None) -> int:
+    parser = argparse.ArgumentParser(
+        prog="gnnc-bench", description="Compile a model and compare its output to torch eager."
+    )
+    parser.add_argument("--model", required=True, choices=available())
+    parser.add_argument("--dataset", default=None,
+                        help="cora | ogbn-arxiv | c1 | c2 | c3 | c3-bf16 | c4; omit for get_inputs()")
+    parser.add_argument("--target", default="b200", choices=("b200", "cpu", "gpu"))
+    parser.add_argument("--dtype", default=None, choices=("fp32", "bf16"),
+                        help="feature dtype on the device (default: the input's)")
+    parser.add_argument("--no-check", action="store_true", help="skip the eager comparison")
+    parser.add_argument("--time", action="store_true", help="time the forward with CUDA events")
+    parser.add_argument("--warmup", type=int, default=20)
+    parser.add_argument("--iters", type=int, default=100)
+    args = parser.parse_args(argv)
+
+    print(f"gnnc-bench {__version__}")
+    print(f"  model    : {args.model}")
+    print(f"  dataset  : {args.dataset or '<synthetic>'}")
+    print(f"  target   : {args.target}")
+    print(f"  DATA_DIR : {paths.DATA_DIR}")
+
+    try:
+        import torch
+
+        from gnnc.compile import compile_executable
+        from gnnc.execution import run_jit
+        from gnnc.ingress import get_model_and_data
+
+        model, forward_inputs = get_model_and_data(MODELS_DIR / f"{args.model}.py", args.dataset)
+        model.eval()
+        if args.dtype == "bf16" and forward_inputs[0].dtype != torch.bfloat16:
+            forward_inputs = (forward_inputs[0].to(torch.bfloat16), *forward_inputs[1:])
+        lowered, results = compile_executable(model, forward_inputs, target=args.target,
+                                              dtype=args.dtype)
+        outs = run_jit(lowered, results, forward_inputs)
+        ref = None
+        if not args.no_check:
+            with torch.no_grad():
+                x = forward_inputs[0]
+                eager_inputs = (x.to(torch.float32), *forward_inputs[1:])
+                ref = model(*eager_inputs).cpu().numpy()
+        timing = _time_forward(lowered, forward_inputs, args.warmup, args.iters) if args.time else None
+    except ImportError as exc:
+        print(f"error: {exc}", file=sys.stderr)
+        return 3
+    except (ValueError, NotImplementedError) as exc:
+        print(f"error: {exc}", file=sys.stderr)
+        return 2
+
+    if len(outs) != 1:
+        print(f"error: multi-output models not yet supported (got {len(outs)})", file=sys.stderr)
+        return 2
+    actual = outs[0].cpu().numpy()
+    if timing:
+        print(f"  forward  : median {timing['median_ms']:.3f} ms, p90 {timing['p90_ms']:.3f} ms")
+    if ref is None:
+        print(f"  out shape: {actual.shape} (not checked)")
+        return 0
+    max_abs = float(np.abs(actual - ref).max())
+    print(f"  out shape: {actual.shape}, max abs diff vs torch: {max_abs:.3e}")
+    bf16 = lowered.program.feature_dtype == torch.bfloat16
+    rtol, atol = (2e-2, 2e-2) if bf16 else (1e-3, 1e-4)
+    try:
+        np.testing.assert_allclose(actual, ref, rtol=rtol, atol=atol)
+    except AssertionError as exc:
+        print("FAIL")
+        print(exc)
+        return 1
+    print("PASS")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

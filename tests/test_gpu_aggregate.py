@@ -1,0 +1,205 @@
+"""Aggregation kernels vs the oracle: GCN SpMM, fused GAT, softmax over given scores.
+
+Covers the reference's known answers, the degree-skew paths (warp rows, CTA
+rows, rows split across CTAs + merge), empty rows, odd widths, bf16 features,
+mean-over-heads, fused activations / log_softmax and run-to-run determinism.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+from conftest import GOLDEN
+from gpu_util import assert_close, random_graph
+
+from oracle import gnn_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _plan(rowptr, cta=0, split=0):
+    from gnnc.b200 import runtime as rt
+
+    return rt.Plan(rowptr, cta_threshold=cta, split_threshold=split)
+
+
+def _csr(device, crow, col):
+    return (torch.as_tensor(np.asarray(crow), dtype=torch.int32, device=device),
+            torch.as_tensor(np.asarray(col), dtype=torch.int32, device=device))
+
+
+@pytest.mark.parametrize("which", ["01", "05"])
+def test_spmm_known_answers(device, which):
+    from gnnc.b200 import runtime as rt
+
+    crow, col, val, b = O.kat_spmm_inputs(which)
+    y = np.load(GOLDEN / "kat_spmm.npz")[f"y{which}"]
+    rowptr, c = _csr(device, crow, col)
+    w = torch.from_numpy(val).to(device)
+    h = rt.empty_rows(b.shape[0], b.shape[1], torch.float32, device)
+    h.copy_(torch.from_numpy(b))
+    out = rt.gcn_aggregate(_plan(rowptr), rowptr, c, w, h)
+    np.testing.assert_allclose(out.cpu().numpy(), y, rtol=1e-6, atol=1e-5)
+
+
+@pytest.mark.parametrize("cta,split", [(0, 0), (2, 4)])
+def test_softmax_spmm_known_answer(device, cta, split):
+    """experiments/gat-gpu-codegen/dumps/cpu.out.txt through gnnc_softmax_aggregate (eps = 0)."""
+    from gnnc.b200 import runtime as rt
+
+    crow, col, val, x = O.kat_softmax_inputs()
+    y = np.load(GOLDEN / "kat_softmax.npz")["y"]
+    rowptr, c = _csr(device, crow, col)
+    h = rt.empty_rows(64, 32, torch.float32, device)
+    h.copy_(torch.from_numpy(x))
+    s = torch.from_numpy(val).to(device).view(-1, 1)
+    out = rt.softmax_aggregate(_plan(rowptr, cta, split), rowptr, c, s, h, heads=1, eps=0.0)
+    np.testing.assert_allclose(out.cpu().numpy(), y, rtol=1e-5, atol=5e-6)
+
+
+def _gcn_case(device, n, e, F, dtype, heavy, cta, split, act, lsm, seed):
+    from gnnc.b200 import runtime as rt
+
+    ei = random_graph(n, e, seed, heavy=heavy)
+    rowptr, col, mult = rt.csr_from_coo(ei.to(device), n, self_loops=True, dedupe=True)
+    _, _, w = rt.gcn_norm(rowptr, col, mult)
+    g = torch.Generator().manual_seed(seed)
+    h_host = torch.randn(n, F, generator=g).to(dtype)
+    h = rt.empty_rows(n, F, dtype, device)
+    h.copy_(h_host)
+    bias = torch.randn(F, generator=g)
+    out = rt.gcn_aggregate(_plan(rowptr, cta, split), rowptr, col, w, h, bias=bias.to(device),
+                           act=act, log_softmax=lsm)
+    ref = O.gcn_rows_fp64(rowptr.cpu(), col.cpu(), w.cpu(), h_host.double(), bias=bias,
+                          act={0: None, 1: "relu", 2: "elu"}[act], log_softmax=lsm)
+    return out, ref
+
+
+@pytest.mark.parametrize(
+    "n,e,F,dtype,heavy,cta,split",
+    [
+        (500, 4000, 7, torch.float32, (), 0, 0),
+        (500, 4000, 47, torch.float32, ((3, 900),), 0, 0),
+        (2000, 30000, 256, torch.float32, ((5, 9000), (9, 300)), 0, 0),
+        (2000, 30000, 256, torch.bfloat16, ((5, 9000),), 0, 0),
+        (3000, 20000, 64, torch.float32, ((1, 700), (2, 70)), 16, 64),
+        (100, 300, 3, torch.float32, (), 1, 2),
+        (700, 6000, 600, torch.float32, (), 0, 0),
+    ],
+)
+def test_gcn_aggregate_matches_oracle(device, n, e, F, dtype, heavy, cta, split):
+    out, ref = _gcn_case(device, n, e, F, dtype, heavy, cta, split, act=1, lsm=False, seed=n + F)
+    assert_close(out, ref)
+
+
+def test_gcn_aggregate_log_softmax_epilogue(device):
+    out, ref = _gcn_case(device, 800, 8000, 47, torch.float32, ((0, 5000),), 0, 0, act=0,
+                         lsm=True, seed=4)
+    assert_close(out, ref)
+
+
+def _gat_case(device, n, e, H, C, dtype, heavy, cta, split, concat, act, lsm, seed,
+              self_loops=True, out_dtype=torch.float32, equal_logits=False):
+    from gnnc.b200 import runtime as rt
+
+    ei = random_graph(n, e, seed, heavy=heavy, loops=0 if not self_loops else 3)
+    rowptr, col, _ = rt.csr_from_coo(ei.to(device), n, self_loops=self_loops, dedupe=False)
+    g = torch.Generator().manual_seed(seed)
+    h_host = torch.randn(n, H * C, generator=g).to(dtype)
+    if equal_logits:
+        asrc = torch.zeros(n, H)
+        adst = torch.zeros(n, H)
+    else:
+        asrc = torch.randn(n, H, generator=g)
+        adst = torch.randn(n, H, generator=g)
+    bias = torch.randn(H * C if concat else C, generator=g)
+    h = rt.empty_rows(n, H * C, dtype, device)
+    h.copy_(h_host)
+    out = rt.gat_aggregate(
+        _plan(rowptr, cta, split), rowptr, col, h, asrc.to(device), adst.to(device), heads=H,
+        concat=concat, bias=bias.to(device), act=act, log_softmax=lsm, out_dtype=out_dtype,
+    )
+    ref = O.gat_rows_fp64(rowptr.cpu(), col.cpu(), h_host.double(), asrc, adst, H, concat=concat,
+                          bias=bias, act={0: None, 1: "relu", 2: "elu"}[act], log_softmax=lsm)
+    return out, ref, rowptr
+
+
+@pytest.mark.parametrize(
+    "n,e,H,C,dtype,heavy,cta,split,concat",
+    [
+        (500, 5000, 1, 7, torch.float32, (), 0, 0, False),
+        (500, 5000, 8, 8, torch.float32, ((3, 600),), 0, 0, True),
+        (2000, 40000, 4, 64, torch.float32, ((5, 20000), (8, 3000)), 0, 0, True),
+        (2000, 40000, 4, 64, torch.bfloat16, ((5, 20000), (8, 3000)), 0, 0, True),
+        (1500, 20000, 4, 64, torch.bfloat16, ((1, 5000),), 32, 128, True),
+        (900, 8000, 3, 5, torch.float32, ((2, 2000),), 8, 64, True),
+        (900, 8000, 3, 5, torch.float32, ((2, 2000),), 8, 64, False),
+        (1200, 9000, 1, 47, torch.float32, ((7, 4500),), 0, 0, False),
+        (600, 6000, 16, 4, torch.float32, (), 0, 0, True),
+        (400, 3000, 2, 128, torch.float32, ((0, 1000),), 0, 0, True),
+    ],
+)
+def test_gat_aggregate_matches_oracle(device, n, e, H, C, dtype, heavy, cta, split, concat):
+    out, ref, _ = _gat_case(device, n, e, H, C, dtype, heavy, cta, split, concat, act=2,
+                            lsm=False, seed=n + H * C)
+    assert_close(out, ref)
+
+
+def test_gat_log_softmax_mean_epilogue(device):
+    out, ref, _ = _gat_case(device, 1000, 9000, 4, 47, torch.float32, ((3, 6000),), 0, 0,
+                            concat=False, act=0, lsm=True, seed=12)
+    assert_close(out, ref)
+
+
+def test_gat_empty_rows_without_self_loops(device):
+    """Nodes with no incoming edge get bias only (PyG scatter_add of nothing)."""
+    out, ref, rowptr = _gat_case(device, 3000, 1500, 2, 16, torch.float32, (), 0, 0, True, act=0,
+                                 lsm=False, seed=21, self_loops=False)
+    deg = rowptr.diff().cpu()
+    assert int((deg == 0).sum()) > 1000
+    assert_close(out, ref)
+
+
+def test_gat_all_equal_logits_is_mean(device):
+    out, ref, _ = _gat_case(device, 800, 6000, 4, 16, torch.float32, ((2, 5000),), 0, 0, True,
+                            act=0, lsm=False, seed=3, equal_logits=True)
+    assert_close(out, ref)
+
+
+def test_gat_bf16_output_within_2e2(device):
+    out, ref, _ = _gat_case(device, 1500, 20000, 4, 64, torch.bfloat16, ((9, 9000),), 0, 0, True,
+                            act=2, lsm=False, seed=8, out_dtype=torch.bfloat16)
+    assert_close(out, ref, rtol=2e-2, atol=2e-2)
+
+
+def test_gat_deterministic_across_runs(device):
+    from gnnc.b200 import runtime as rt
+
+    n = 3000
+    ei = random_graph(n, 60000, 5, heavy=((1, 15000), (2, 2500)))
+    rowptr, col, _ = rt.csr_from_coo(ei.to(device), n, self_loops=True, dedupe=False)
+    plan = _plan(rowptr)
+    assert plan.info()["n_split_rows"] == 1 and plan.info()["n_cta_rows"] >= 1
+    h = torch.randn(n, 256, device=device).to(torch.bfloat16)
+    asrc = torch.randn(n, 4, device=device)
+    adst = torch.randn(n, 4, device=device)
+    a = rt.gat_aggregate(plan, rowptr, col, h, asrc, adst, heads=4)
+    b = rt.gat_aggregate(plan, rowptr, col, h, asrc, adst, heads=4)
+    assert torch.equal(a.view(torch.int32), b.view(torch.int32))
+
+
+def test_bad_column_is_skipped_and_reported(device):
+    """A column index past the feature table is never dereferenced; the kernel
+    flags it and gnnc_synchronize reports GNNC_ERR_BOUNDS."""
+    from gnnc.b200 import runtime as rt
+    from gnnc.b200._lib import GnncInvalidArgument
+
+    rowptr = torch.tensor([0, 2, 3], dtype=torch.int32, device=device)
+    col = torch.tensor([0, 1, 1000], dtype=torch.int32, device=device)
+    w = torch.ones(3, device=device)
+    h = torch.ones(4, 8, device=device)
+    rt.gcn_aggregate(_plan(rowptr), rowptr, col, w, h)
+    with pytest.raises(GnncInvalidArgument):
+        rt.Context.get(device).synchronize()
+    rt.Context.get(device).synchronize()  # flag cleared

@@ -1,0 +1,119 @@
+"""Host-side logic: phase pipeline, lowering, CLI exit codes, synthetic workloads."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from gnnc.compile import lower
+from gnnc.examples import MODELS_DIR, available
+from gnnc.ingress import get_model_and_data
+from gnnc.pipeline.phase import PhaseNotReached, PhasePipeline
+
+
+def test_available_models():
+    assert available() == ["gat", "gcn"]
+
+
+def test_phase_pipeline_stop_and_print():
+    p = PhasePipeline()
+    p.add_callable_phase("a", lambda m: m + 1, ("inc",))
+    p.add_callable_phase("b", lambda m: m * 10, ("mul",))
+    p.add_callable_phase("c", lambda m: m - 3)
+    assert p.run(1)[0] == 17
+    mod, trace = p.run(1, stop_after="b")
+    assert mod == 20 and [t[0] for t in trace] == ["a", "b"]
+    assert p.run(1, stop_before="b")[0] == 2
+    seen = []
+    p.run(1, print_ir_after=frozenset({"a"}), emit=seen.append)
+    assert "IR after a" in seen[0] and seen[0].endswith("2")
+    with pytest.raises(PhaseNotReached):
+        p.run(1, stop_after="zz")
+    with pytest.raises(PhaseNotReached):
+        p.run(1, stop_before="b", print_ir_after=frozenset({"c"}))
+    with pytest.raises(ValueError):
+        p.run(1, stop_before="a", stop_after="b")
+    with pytest.raises(ValueError):
+        p.add_callable_phase("a", lambda m: m)
+
+
+@pytest.mark.parametrize("model_name", ["gcn", "gat"])
+def test_lowering_fuses_epilogues(model_name):
+    model, inputs = get_model_and_data(MODELS_DIR / f"{model_name}.py")
+    prog, trace = lower(model, inputs, stop_after="b200-lower")
+    assert [t[0] for t in trace] == ["import", "b200-lower"]
+    assert [layer.kind for layer in prog.layers] == [model_name, model_name]
+    first, last = prog.layers
+    assert first.act == (1 if model_name == "gcn" else 2)  # relu / elu
+    assert last.log_softmax and not first.log_softmax
+    if model_name == "gat":
+        assert first.heads == 2 and first.concat and not last.concat
+
+
+def test_lowering_rejects_unsupported_ops():
+    from gnnc.nn import GCNConv
+
+    class Odd(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.conv = GCNConv(4, 4, normalize=False)
+
+        def forward(self, x, adj):
+            return torch.tanh(self.conv(x, adj))
+
+    with pytest.raises(NotImplementedError):
+        lower(Odd(), (torch.randn(3, 4), None), stop_after="b200-lower")
+
+
+def test_mlir_targets_are_import_errors():
+    model, inputs = get_model_and_data(MODELS_DIR / "gcn.py")
+    with pytest.raises(ImportError):
+        lower(model, inputs, target="cpu")
+    with pytest.raises(NotImplementedError):
+        lower(model, inputs, target="tpu")
+
+
+def test_bench_cli_exit_codes(capsys):
+    from gnnc.tools.gnnc_bench import main
+
+    assert main(["--model", "gcn", "--target", "cpu"]) == 3
+    assert main(["--model", "gat", "--dataset", "c1"]) == 2  # c1 is a GCN workload
+
+
+def test_synthetic_c1_exact_shape_and_deterministic():
+    from gnnc.examples import synthetic as S
+
+    cfg = S.CONFIGS["c1"]
+    ei = S.make_graph(cfg)
+    assert ei.shape == (2, 10556)
+    assert int((ei[0] == ei[1]).sum()) == 0
+    keys = ei[0] * cfg.num_nodes + ei[1]
+    assert torch.unique(keys).numel() == 10556
+    # symmetric
+    rev = ei[1] * cfg.num_nodes + ei[0]
+    assert torch.equal(torch.sort(keys).values, torch.sort(rev).values)
+    assert torch.equal(ei, S.make_graph(cfg))
+    x = S.make_features(cfg)
+    assert x.shape == (2708, 1433) and set(torch.unique(x).tolist()) <= {0.0, 1.0}
+    assert abs(x.mean().item() - 0.0127) < 0.002
+
+
+def test_synthetic_rmat_unique_count():
+    from gnnc.examples import synthetic as S
+
+    ei, m = S.rmat_unique_symmetric(1000, 5000, seed=3)
+    assert m == 5000
+    assert int((ei[0] == ei[1]).sum()) == 0
+    assert ei.max() < 1000
+    keys = ei[0] * 1000 + ei[1]
+    assert torch.unique(keys).numel() == ei.size(1)
+
+
+def test_config_model_power_law_tail():
+    from gnnc.examples import synthetic as S
+
+    ei = S.config_model_edges(20000, 100000, 2.1, seed=7)
+    assert ei.size(1) == 200000
+    deg = np.bincount(ei[1].numpy(), minlength=20000)
+    assert deg.max() > 20 * deg.mean()  # heavy tail
