@@ -91,10 +91,12 @@ class B200Program:
     layers: list[LayerOp]
     input_names: list[str]
     feature_dtype: torch.dtype = torch.float32
+    output_dtype: torch.dtype = torch.float32
     notes: list[str] = field(default_factory=list)
 
     def __str__(self) -> str:
-        lines = [f"b200.program(inputs={self.input_names}, features={self.feature_dtype})"]
+        lines = [f"b200.program(inputs={self.input_names}, features={self.feature_dtype}, "
+                 f"output={self.output_dtype})"]
         lines += [layer.describe() for layer in self.layers]
         return "\n".join(lines)
 
@@ -138,7 +140,8 @@ _LOGSM = {F.log_softmax, torch.log_softmax}
 _DROPOUT = {F.dropout, torch.nn.functional.dropout}
 
 
-def lower_graph(gm: fx.GraphModule, feature_dtype: torch.dtype | None = None) -> B200Program:
+def lower_graph(gm: fx.GraphModule, feature_dtype: torch.dtype | None = None,
+                output_dtype: torch.dtype | None = None) -> B200Program:
     """Matches the conv / activation chain of `gm` into a B200Program."""
     modules = dict(gm.named_modules())
     placeholders: list[str] = []
@@ -236,7 +239,8 @@ def lower_graph(gm: fx.GraphModule, feature_dtype: torch.dtype | None = None) ->
         if prev.out_width != nxt.in_channels:
             raise ValueError(f"{nxt.name} expects {nxt.in_channels} features, gets {prev.out_width}")
     return B200Program(layers=layers, input_names=placeholders,
-                       feature_dtype=feature_dtype or torch.float32)
+                       feature_dtype=feature_dtype or torch.float32,
+                       output_dtype=output_dtype or torch.float32)
 
 
 # ---------------------------------------------------------------------------
@@ -373,7 +377,7 @@ class B200Executable:
             for i, (layer, (w, asrc_w, adst_w, bias)) in enumerate(zip(layers, self._weights, strict=True)):
                 g = self._graph_for(graph, n, layer)
                 last = i == len(layers) - 1
-                out_dtype = torch.float32 if last else dt
+                out_dtype = self.program.output_dtype if last else dt
                 if layer.kind == "gcn":
                     h = rt.proj(h_in, w, out_dtype=dt)
                     h_in = rt.gcn_aggregate(
@@ -396,5 +400,10 @@ class B200Executable:
         x, graph = inputs
         out = self.run_device(x, graph)
         if not x.is_cuda:
-            return [out.to("cpu")]
+            # Pinned host result: the DMA runs at full PCIe rate and torch's
+            # pinned caching allocator recycles the buffer across calls.
+            host = torch.empty(tuple(out.shape), dtype=out.dtype, pin_memory=True)
+            host.copy_(out, non_blocking=True)
+            torch.cuda.current_stream(self.device).synchronize()
+            return [host]
         return [out.contiguous()]

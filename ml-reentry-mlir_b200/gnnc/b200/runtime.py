@@ -274,11 +274,16 @@ def proj(
     att_dst: torch.Tensor | None = None,
     heads: int = 1,
     out_dtype: torch.dtype | None = None,
+    out: torch.Tensor | None = None,
+    asrc_out: torch.Tensor | None = None,
+    adst_out: torch.Tensor | None = None,
 ):
     """h = x . weight^T (+ GAT attention coefficients).
 
     x [N,K] (fp32 or bf16, padded rows allowed); weight [F,K] same dtype.
     Returns h [N,F] (row-padded) or (h, asrc [N,H], adst [N,H]) when att_* given.
+    out / asrc_out / adst_out: optional destination tensors (e.g. this rank's
+    slot of an all-gather buffer).
     """
     _check_cuda(x, weight, att_src, att_dst)
     if x.dtype != weight.dtype:
@@ -288,12 +293,14 @@ def proj(
     if weight.size(1) != K:
         raise ValueError(f"weight is {tuple(weight.shape)}, x has {K} columns")
     out_dtype = out_dtype or x.dtype
-    h = empty_rows(N, F, out_dtype, x.device)
+    h = _out(N, F, out_dtype, x.device, out)
     att = att_src is not None
     asrc = adst = None
     if att:
-        asrc = torch.empty((N, heads), dtype=torch.float32, device=x.device)
-        adst = torch.empty((N, heads), dtype=torch.float32, device=x.device)
+        asrc = asrc_out if asrc_out is not None else torch.empty((N, heads), dtype=torch.float32, device=x.device)
+        adst = adst_out if adst_out is not None else torch.empty((N, heads), dtype=torch.float32, device=x.device)
+        if asrc.shape != (N, heads) or adst.shape != (N, heads) or not (asrc.is_contiguous() and adst.is_contiguous()):
+            raise ValueError("asrc_out / adst_out must be contiguous [N, heads] fp32")
         att_src = att_src.reshape(-1).to(torch.float32).contiguous()
         att_dst = att_dst.reshape(-1).to(torch.float32).contiguous()
     Context.get(x.device).call(

@@ -62,13 +62,22 @@ def lower(
     print_ir_after: frozenset[str] = frozenset(),
     emit=print,
     dtype=None,
+    out_dtype=None,
     device=None,
 ):
-    """Run the phase pipeline, halting per `stop_*`. Returns `(module, trace)`."""
+    """Run the phase pipeline, halting per `stop_*`. Returns `(module, trace)`.
+
+    dtype: feature dtype on the device ("fp32" / "bf16" / torch dtype; default
+    the input's); out_dtype: dtype of the returned output (default float32)."""
     _check_target(target)
     pipeline = _frontend_pipeline(model)
     pipeline.extend(
-        build_pipeline(target=target, feature_dtype=_feature_dtype(forward_inputs, dtype), device=device)
+        build_pipeline(
+            target=target,
+            feature_dtype=_feature_dtype(forward_inputs, dtype),
+            output_dtype=_feature_dtype(forward_inputs, out_dtype) if out_dtype else None,
+            device=device,
+        )
     )
     return pipeline.run(
         None,
@@ -87,13 +96,15 @@ def compile_executable(
     *,
     target: str = "b200",
     dtype=None,
+    out_dtype=None,
     device=None,
 ):
     """Compile `model` for `target`; returns `(lowered, results)`.
 
     `lowered` is a B200Executable; `results` lists the output's (shape, dtype),
     the analogue of the entry function's result types in the reference."""
-    lowered, _ = lower(model, forward_inputs, target=target, dtype=dtype, device=device)
+    lowered, _ = lower(model, forward_inputs, target=target, dtype=dtype, out_dtype=out_dtype,
+                       device=device)
     n = forward_inputs[0].size(0)
     width = lowered.program.layers[-1].out_width
-    return lowered, [((n, width), torch.float32)]
+    return lowered, [((n, width), lowered.program.output_dtype)]

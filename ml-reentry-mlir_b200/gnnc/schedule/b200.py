@@ -16,7 +16,11 @@ from gnnc.pipeline.phase import PhasePipeline
 
 
 def build_pipeline(
-    *, target: str, feature_dtype: torch.dtype | None = None, device=None
+    *,
+    target: str,
+    feature_dtype: torch.dtype | None = None,
+    output_dtype: torch.dtype | None = None,
+    device=None,
 ) -> PhasePipeline:
     if target != "b200":
         raise NotImplementedError(f"target {target!r} not supported by this schedule")
@@ -25,7 +29,7 @@ def build_pipeline(
     pipeline = PhasePipeline()
     pipeline.add_callable_phase(
         "b200-lower",
-        lambda gm: lower_graph(gm, feature_dtype),
+        lambda gm: lower_graph(gm, feature_dtype, output_dtype),
         ("match-conv-chain", "fuse-bias-activation", "fuse-log-softmax"),
     )
     pipeline.add_callable_phase(

@@ -248,6 +248,36 @@ def gat_rows_fp64(
     return torch.cat(outs) if outs else torch.empty((0, Fw if concat else C), dtype=torch.float64)
 
 
+def gat_layer_sample(x_rows, weight, att_src, att_dst, bias, heads, channels, h_src, asrc_src,
+                     rowptr, col, negative_slope=0.2):
+    """The CPU-baseline sample of one GAT layer: PyG's op sequence for the
+    destination rows [0, R) (R = len(x_rows)), including those rows' share of
+    the projection. h_src / asrc_src are the projected features of every
+    source node (computed once, outside the timing) that the edges gather.
+
+    Work per call = R rows of projection + the E_R = rowptr[R] edges of the
+    edge chain (gat.1-raw-torch.mlir:5-129, restricted to the sample)."""
+    H, C = heads, channels
+    R = x_rows.size(0)
+    h = (x_rows @ weight.t()).view(-1, H, C)  # this sample's share of aten.linear
+    a_dst = (h * att_dst.view(1, H, C)).sum(dim=-1)
+    e_r = int(rowptr[R])
+    src = torch.as_tensor(col[:e_r], dtype=torch.int64)
+    dst = torch.repeat_interleave(torch.arange(R), torch.as_tensor(rowptr[: R + 1]).diff())
+    e = F.leaky_relu(asrc_src.index_select(0, src) + a_dst.index_select(0, dst), negative_slope)
+    idx = dst.view(-1, 1).expand_as(e)
+    m = e.new_zeros((R, H)).scatter_reduce(0, idx, e.detach(), "amax", include_self=False)
+    p = (e - m.index_select(0, dst)).exp()
+    s = e.new_zeros((R, H)).scatter_add(0, idx, p) + 1e-16
+    alpha = p / s.index_select(0, dst)
+    msg = alpha.unsqueeze(-1) * h_src.view(-1, H, C).index_select(0, src)
+    out = h.new_zeros((R, H, C)).scatter_add(0, dst.view(-1, 1, 1).expand_as(msg), msg)
+    out = out.view(-1, H * C)
+    if bias is not None:
+        out = out + bias
+    return F.elu(out)
+
+
 def gcn_rows_fp64(rowptr, col, w, h, *, rows=None, bias=None, act=None, log_softmax=False):
     """GCN aggregation of given h in float64 for destination rows `rows`."""
     rowptr = torch.as_tensor(rowptr, dtype=torch.int64)

@@ -29,6 +29,16 @@ def _run(model_name, dataset, dtype=None):
     return model, inputs, out
 
 
+def assert_argmax_agrees(out: torch.Tensor, ref: torch.Tensor, tol: float) -> None:
+    """Predictions agree exactly on every row whose oracle top-2 margin exceeds
+    the numeric tolerance (closer pairs are ties within floating-point noise)."""
+    top2 = ref.topk(2, dim=1).values
+    decided = (top2[:, 0] - top2[:, 1]) > 2 * tol
+    a, b = out.argmax(1), ref.argmax(1)
+    bad = int((a[decided] != b[decided]).sum())
+    assert bad == 0, f"{bad} decided rows disagree ({int((~decided).sum())} near-ties excluded)"
+
+
 def _oracle(model_name, model, inputs):
     x, graph = inputs
     if model_name == "gcn":
@@ -44,7 +54,7 @@ def test_compile_matches_oracle(device, model_name, dataset):
     model, inputs, out = _run(model_name, dataset)
     ref = _oracle(model_name, model, inputs)
     np.testing.assert_allclose(out.numpy(), ref.numpy(), rtol=1e-4, atol=1e-4)
-    assert torch.equal(out.argmax(1), ref.argmax(1))
+    assert_argmax_agrees(out, ref, 1e-4)
 
 
 def test_compile_matches_eager_model(device):
@@ -61,5 +71,4 @@ def test_c3_rmat_three_layer_gat(device, dataset, dtype, tol):
     x, ei = inputs
     ref = O.gat_forward(model, x.to(torch.float32), ei)
     np.testing.assert_allclose(out.numpy(), ref.numpy(), rtol=tol, atol=tol)
-    agree = (out.argmax(1) == ref.argmax(1)).float().mean().item()
-    assert agree == 1.0 if dtype is None and dataset == "c3" else agree > 0.99
+    assert_argmax_agrees(out, ref, tol)
