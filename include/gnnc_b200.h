@@ -219,6 +219,34 @@ GNNC_API int gnnc_softmax_aggregate(gnnc_ctx_t* ctx, const gnnc_plan_t* plan, co
                            float eps, int concat, const float* bias, int act, int log_softmax,
                            void* out, int out_dtype, int64_t ldo);
 
+/* gnnc_gat_aggregate for callers that must not allocate device memory.
+ * This entry point has no counterpart in the reference.
+ * Who needs it: a serving process that reserves its whole memory budget at
+ * start-up (a cudaMalloc in the middle of a request can fail because the
+ * device is already full, and cudaMalloc / cudaFree synchronise the device),
+ * or a host runtime that owns all device memory through its own pool and
+ * forbids libraries from allocating behind its back. gnnc_gat_aggregate may
+ * grow the context workspace with cudaMalloc; this variant never calls
+ * cudaMalloc, cudaFree or any allocating routine.
+ * Same arguments and results as gnnc_gat_aggregate. Its scratch (work
+ * counters, the bad-index flag, split-row partials) is one fixed 16 MiB device
+ * array inside the library, held by every GPU that loads the library until
+ * the process exits. A plan whose split rows need more than 16 MiB - 256 B of
+ * partials (n_segments * (32 + F_pad) * 4 bytes) is rejected with
+ * GNNC_ERR_UNSUPPORTED before anything is launched.
+ * The first call on a device looks up the array's device address (once per
+ * device, that device current); make that first call before any stream
+ * capture. All calls on a device share the one array: calls that overlap on
+ * the GPU (different streams or contexts of the same device) race and give
+ * wrong results; serialise them. */
+GNNC_API int gnnc_gat_aggregate_noalloc(gnnc_ctx_t* ctx, const gnnc_plan_t* plan,
+                                        const int32_t* rowptr, const int32_t* col, const void* h,
+                                        int h_dtype, int64_t ldh, const float* asrc,
+                                        const float* adst, int64_t n_rows, int64_t n_src,
+                                        int64_t H, int64_t C, float negative_slope, int concat,
+                                        const float* bias, int act, int log_softmax, void* out,
+                                        int out_dtype, int64_t ldo);
+
 #ifdef __cplusplus
 }
 #endif

@@ -32,6 +32,7 @@
 //  * Epilogue, fused: divide by the softmax denominator, concat or mean over
 //    heads, + bias, ReLU / ELU, optional row log_softmax, convert, store.
 #include <algorithm>
+#include <mutex>
 #include <vector>
 
 #include "common.cuh"
@@ -805,4 +806,145 @@ extern "C" int gnnc_softmax_aggregate(gnnc_ctx_t* ctx, const gnnc_plan_t* plan,
   return gat_like(ctx, plan, MODE_SCORES, rowptr, col, s, h, h_dtype, ldh, nullptr, nullptr,
                   n_rows, n_src, H, C, 0.f, eps, concat, bias, act, log_softmax, out, out_dtype,
                   ldo);
+}
+
+// ---------------------------------------------------------------------------
+// GAT aggregation that allocates nothing
+// ---------------------------------------------------------------------------
+// Some callers cannot allocate device memory while a layer runs: a serving
+// process that reserves its whole memory budget at start-up (a cudaMalloc in
+// the middle of a request can fail because the device is already full, and
+// cudaMalloc / cudaFree synchronise the device), or a host runtime that owns
+// all device memory through its own pool and forbids libraries from
+// allocating behind its back. gnnc_gat_aggregate may grow the context
+// workspace with cudaMalloc when a plan needs more split-row partials than it
+// has seen before; gnnc_gat_aggregate_noalloc never allocates. Its scratch -
+// the scheduling counters, the bad-index flag and the split-row partials -
+// lives in the fixed array below, which every GPU that loads this library
+// holds until the process exits.
+
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(16) << 20;  // 16 MiB per device
+constexpr size_t kStaticCounterBytes = 256;               // counters first, partials after
+
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+std::mutex g_static_mu;
+void* g_static_addr[256] = {};  // device address of g_static_scratch, per device
+
+// Looks up (once per device, with that device current) the device address of
+// g_static_scratch. In host code the array's name is only a host-side stand-in,
+// so kernels get this address instead.
+int static_scratch(gnnc_ctx_t* ctx, unsigned char** out) {
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (ctx->device < 0 || ctx->device >= 256)
+    return gnnc::set_error(ctx, GNNC_ERR_UNSUPPORTED, "device index %d out of range", ctx->device);
+  if (!g_static_addr[ctx->device]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return gnnc::cuda_status(ctx, e, "cudaGetSymbolAddress(static scratch)");
+    g_static_addr[ctx->device] = p;
+  }
+  *out = reinterpret_cast<unsigned char*>(g_static_addr[ctx->device]);
+  return GNNC_OK;
+}
+
+// ORs the call's bad-index flag into the context's flag word, which
+// gnnc_synchronize reports.
+__global__ void fold_flag_kernel(const int* from, int* into) {
+  if (*from) atomicOr(into, 1);
+}
+
+}  // namespace
+
+extern "C" int gnnc_gat_aggregate_noalloc(gnnc_ctx_t* ctx, const gnnc_plan_t* plan,
+                                          const int32_t* rowptr, const int32_t* col,
+                                          const void* h, int h_dtype, int64_t ldh,
+                                          const float* asrc, const float* adst, int64_t n_rows,
+                                          int64_t n_src, int64_t H, int64_t C,
+                                          float negative_slope, int concat, const float* bias,
+                                          int act, int log_softmax, void* out, int out_dtype,
+                                          int64_t ldo) {
+  if (!ctx) return GNNC_ERR_INVALID;
+  GNNC_CHECK_ARG(ctx, H >= 1 && C >= 1, "bad heads/channels");
+  if (H > kHMax)
+    return gnnc::set_error(ctx, GNNC_ERR_UNSUPPORTED, "at most %d heads supported", kHMax);
+  const int64_t F = H * C, F_out = concat ? F : C;
+  int st = check_common(ctx, plan, rowptr, col, h, h_dtype, ldh, n_rows, n_src, F, act, out,
+                        out_dtype, ldo, F_out);
+  if (st) return st;
+  if (n_rows == 0) return GNNC_OK;
+  GNNC_CHECK_ARG(ctx, asrc && adst, "null attention coefficients");
+  GNNC_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  unsigned char* scratch = nullptr;
+  st = static_scratch(ctx, &scratch);
+  if (st) return st;
+
+  AggParams p = base_params(plan);
+  p.rowptr = rowptr; p.col = col; p.scores = nullptr; p.asrc = asrc; p.adst = adst;
+  p.h = h; p.ldh = ldh; p.n_rows = n_rows; p.n_src = n_src;
+  p.H = int(H); p.C = int(C); p.F = int(F); p.F_out = int(F_out);
+  p.mode = MODE_GAT; p.concat = concat; p.act = act; p.log_softmax = log_softmax;
+  p.slope = negative_slope; p.eps = 1e-16f; p.bias = bias; p.out = out; p.out_dtype = out_dtype;
+  p.ldo = ldo;
+
+  // Same kernel choice as gnnc_gat_aggregate.
+  const int vmax = h_dtype == GNNC_BF16 ? 8 : 4;
+  const bool heads_ok = p.H == 1 || (p.C % vmax == 0);
+  const bool align_ok = (reinterpret_cast<uintptr_t>(h) % 16 == 0) && (ldh % vmax == 0);
+  const int vec = (heads_ok && align_ok) ? vmax : 1;
+  int lpg, nv;
+  row_layout(p.F, vec, &lpg, &nv);
+  if (nv > 8)
+    return gnnc::set_error(ctx, GNNC_ERR_UNSUPPORTED,
+                           "feature width %d too large for the row kernel (vector width %d)", p.F,
+                           vec);
+  KernelFn fn = nullptr;
+  if (h_dtype == GNNC_BF16)
+    fn = vec == 8 ? pick_layout<__nv_bfloat16, 8>(lpg, nv) : pick_layout<__nv_bfloat16, 1>(lpg, nv);
+  else
+    fn = vec == 4 ? pick_layout<float, 4>(lpg, nv) : pick_layout<float, 1>(lpg, nv);
+  if (!fn) return gnnc::set_error(ctx, GNNC_ERR_UNSUPPORTED, "no kernel for layout");
+  p.F_pad = int(gnnc::align_up(size_t(lpg * vec * nv), 4));
+  p.HS = p.H;
+  p.part_stride = part_stride_floats(p.F_pad);
+  p.cta_items = plan->cta_items;
+  p.n_cta_items = plan->n_cta_items;
+  p.split_rows = plan->split_rows;
+  p.warp_tasks = plan->warp_tasks;
+  p.n_warp_tasks = plan->n_warp_tasks;
+  p.cta_threshold = plan->cta_threshold;
+
+  const size_t need = size_t(plan->n_segments) * p.part_stride * sizeof(float);
+  if (need > kStaticScratchBytes - kStaticCounterBytes)
+    return gnnc::set_error(ctx, GNNC_ERR_UNSUPPORTED,
+                           "this plan's %lld split-row segments need %zu bytes of scratch; the "
+                           "fixed scratch holds %zu (raise split_threshold or use "
+                           "gnnc_gat_aggregate)",
+                           (long long)plan->n_segments, need,
+                           kStaticScratchBytes - kStaticCounterBytes);
+  p.counters = reinterpret_cast<int*>(scratch);
+  p.partials = reinterpret_cast<float*>(scratch + kStaticCounterBytes);
+
+  const size_t smem = agg_smem_bytes(p.F_pad, p.HS);
+  if (smem > 48 * 1024)
+    GNNC_CUDA_TRY(ctx, cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            int(smem)));
+  int per_sm = 0;
+  GNNC_CUDA_TRY(ctx, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, smem));
+  if (per_sm < 1) per_sm = 1;
+  // The array keeps the previous call's contents: the two work counters and
+  // the bad-index flag must start at zero. Partials are written before read.
+  GNNC_CUDA_TRY(ctx, cudaMemsetAsync(p.counters, 0, 3 * sizeof(int), ctx->stream));
+  fn<<<ctx->num_sms * per_sm, kThreads, smem, ctx->stream>>>(p);
+  GNNC_CUDA_TRY(ctx, cudaGetLastError());
+  if (plan->n_split_rows > 0) {
+    const size_t msmem = sizeof(float) * (p.F_pad + 2 * kHMax);
+    merge_kernel<<<unsigned(plan->n_split_rows), kThreads, msmem, ctx->stream>>>(p);
+    GNNC_CUDA_TRY(ctx, cudaGetLastError());
+  }
+  fold_flag_kernel<<<1, 1, 0, ctx->stream>>>(p.counters + 2, ctx->dev_words + 2);
+  GNNC_CUDA_TRY(ctx, cudaGetLastError());
+  return GNNC_OK;
 }

@@ -69,6 +69,13 @@ SIGNATURES: dict[str, tuple] = {
             _P, c_int, c_int, _P, c_int, _I64,
         ],
     ),
+    "gnnc_gat_aggregate_noalloc": (
+        c_int,
+        [
+            _P, _P, _P, _P, _P, c_int, _I64, _P, _P, _I64, _I64, _I64, _I64, c_float, c_int,
+            _P, c_int, c_int, _P, c_int, _I64,
+        ],
+    ),
     "gnnc_softmax_aggregate": (
         c_int,
         [

@@ -27,6 +27,7 @@ __all__ = [
     "csr_from_coo",
     "empty_rows",
     "gat_aggregate",
+    "gat_aggregate_noalloc",
     "gcn_aggregate",
     "gcn_norm",
     "proj",
@@ -425,5 +426,52 @@ def softmax_aggregate(
         plan.handle, rowptr.data_ptr(), col.data_ptr(), scores.data_ptr(), h.data_ptr(), _dt(h),
         _ld(h), n_rows, h.size(0), heads, C, float(eps), int(concat), _p(bias), act,
         int(log_softmax), out.data_ptr(), _dt(out), _ld(out),
+    )
+    return out
+
+
+def gat_aggregate_noalloc(
+    plan: Plan,
+    rowptr: torch.Tensor,
+    col: torch.Tensor,
+    h: torch.Tensor,
+    asrc: torch.Tensor,
+    adst: torch.Tensor,
+    out: torch.Tensor,
+    *,
+    heads: int,
+    negative_slope: float = 0.2,
+    concat: bool = True,
+    bias: torch.Tensor | None = None,
+    act: int = ACT_NONE,
+    log_softmax: bool = False,
+) -> torch.Tensor:
+    """gat_aggregate for callers that must not allocate device memory mid-run
+    (a process that reserved its memory budget up front, or a runtime that owns
+    all device memory through its own pool). The library call allocates
+    nothing: its scratch is a fixed 16 MiB array inside the library, shared by
+    every call on the device, so calls must not overlap on the GPU. The caller
+    passes every input and the output `out` (its dtype picks the output dtype)."""
+    _check_cuda(rowptr, col, h, asrc, adst, bias, out)
+    n_rows = rowptr.numel() - 1
+    F = h.size(1)
+    if F % heads:
+        raise ValueError("feature width not divisible by heads")
+    C = F // heads
+    width = F if concat else C
+    if tuple(out.shape) != (n_rows, width):
+        raise ValueError(f"out must be [{n_rows},{width}]")
+    _check_edges(plan, col)
+    if asrc.shape != (h.size(0), heads) or adst.shape != (n_rows, heads):
+        raise ValueError("asrc must be [n_src, heads] and adst [n_rows, heads]")
+    if not (asrc.is_contiguous() and adst.is_contiguous()):
+        raise ValueError("asrc and adst must be contiguous")
+    if bias is not None and not (bias.dtype == torch.float32 and bias.is_contiguous()):
+        raise ValueError("bias must be a contiguous float32 tensor")
+    plan.ctx.call(
+        "gnnc_gat_aggregate_noalloc",
+        plan.handle, rowptr.data_ptr(), col.data_ptr(), h.data_ptr(), _dt(h), _ld(h),
+        asrc.data_ptr(), adst.data_ptr(), n_rows, h.size(0), heads, C, float(negative_slope),
+        int(concat), _p(bias), act, int(log_softmax), out.data_ptr(), _dt(out), _ld(out),
     )
     return out
