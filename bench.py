@@ -179,10 +179,17 @@ def make_layer_module():
     return GATLayer().eval()
 
 
-def host_workload():
+def host_workload(scale: float = 1.0):
+    """The c4 graph and features; scale < 1 shrinks nodes and edges proportionally
+    (smaller captures for profiling; the headline always uses scale 1)."""
+    import dataclasses
+
     from gnnc.examples import synthetic as S
 
     cfg = S.CONFIGS["c4-gat"]
+    if scale != 1.0:
+        cfg = dataclasses.replace(cfg, num_nodes=int(cfg.num_nodes * scale),
+                                  num_edges=int(cfg.num_edges * scale))
     t0 = time.time()
     ei = S.make_graph(cfg)
     x = S.make_features(cfg)
@@ -190,10 +197,10 @@ def host_workload():
     return cfg, ei, x
 
 
-def broadcast_workload(rank, world, device):
+def broadcast_workload(rank, world, device, scale=1.0):
     """Rank 0 generates the graph and features; every rank receives them over NCCL."""
     if rank == 0:
-        cfg, ei, x = host_workload()
+        cfg, ei, x = host_workload(scale)
         shape = torch.tensor([ei.size(1), x.size(0)], dtype=torch.int64, device=device)
     else:
         from gnnc.examples import synthetic as S
@@ -230,7 +237,7 @@ def run_b200(args) -> None:
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
 
-    cfg, ei_host, x_host, ei_d, x_d = broadcast_workload(rank, world, device)
+    cfg, ei_host, x_host, ei_d, x_d = broadcast_workload(rank, world, device, args.scale)
     N = x_d.size(0)
     rowptr, col, _ = rt.csr_from_coo(ei_d, N, self_loops=True, dedupe=False)
     del ei_d
@@ -345,7 +352,7 @@ def run_b200(args) -> None:
             "data": "synthetic (seeded configuration-model power-law graph and N(0,1) features "
                     "with the c4 shapes; no dataset content)",
             "config": {
-                "workload": WORKLOAD,
+                "workload": WORKLOAD if args.scale == 1.0 else f"{WORKLOAD} scaled x{args.scale}",
                 "layer": "GATConv(100 -> 4x64, concat) + ELU, bf16 features, fp32 accumulation",
                 "nodes": N,
                 "edges": E,
@@ -580,6 +587,8 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--scale", type=float, default=1.0,
+                    help="shrink the graph (profiling captures only; not a bench line)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         log("[bench] warmup raised to 3 (minimum)")

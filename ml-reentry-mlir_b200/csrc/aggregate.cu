@@ -60,6 +60,7 @@ struct AggParams {
   int H, C, F, F_pad, HS;
   float slope, eps;
   int mode, concat, act, log_softmax;
+  int fast_epilogue;  // concat, no log_softmax, vector-aligned out/bias: register epilogue
   const float* bias;
   void* out;
   int out_dtype;
@@ -149,17 +150,57 @@ __device__ void warp_epilogue(const AggParams& p, int64_t row, const float* s_ro
   }
 }
 
+// Warp-wide max of a float in one instruction (sm_100a redux.sync).
+__device__ __forceinline__ float warp_max_redux(float v) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&b);
+}
+
+// Stores VEC consecutive outputs of one row: one 16/8-byte store when VEC >= 4.
+template <int VEC>
+__device__ __forceinline__ void store_vec(void* out, int dtype, size_t idx, const float* v) {
+  if (dtype == GNNC_BF16) {
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + idx;
+    if constexpr (VEC == 8) {
+      *reinterpret_cast<uint4*>(o) = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                                                pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+    } else if constexpr (VEC == 4) {
+      *reinterpret_cast<uint2*>(o) = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
+    } else {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[e] = __float2bfloat16_rn(v[e]);
+    }
+  } else {
+    float* o = reinterpret_cast<float*>(out) + idx;
+    if constexpr (VEC % 4 == 0) {
+#pragma unroll
+      for (int e = 0; e < VEC; e += 4)
+        *reinterpret_cast<float4*>(o + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[e] = v[e];
+    }
+  }
+}
+
 template <typename TH, int VEC, int LPG, int NV>
 struct Agg {
   static constexpr int G = 32 / LPG;  // edge groups per warp
   static constexpr int U = NV == 1 ? 4 : (NV == 2 ? 2 : 1);
 
-  // Accumulates edges [eb, ee) of `row`. Per-head running max / sum live in
-  // lane hd (m_reg, s_reg); acc is the group-partial weighted sum.
+  // Accumulates edges [eb, ee) of `row`. The running per-head max lives in
+  // lane hd (m_reg); acc and s_acc (the exp-sum of the lane's head) are the
+  // group-partial weighted sums.
   static __device__ __forceinline__ void range(const AggParams& p, int64_t row, int eb, int ee,
-                                               float (&acc)[NV][VEC], float& m_reg, float& s_reg,
-                                               int32_t* s_col, float* s_p, const int (&hv)[NV],
-                                               int lane) {
+                                               float (&acc)[NV][VEC], float (&s_acc)[NV],
+                                               float& m_reg, int32_t* s_col, float* s_p,
+                                               const int (&hv)[NV], int lane) {
     const int lig = lane % LPG;
     const int grp = lane / LPG;
     const char* hbase = reinterpret_cast<const char*>(p.h);
@@ -198,16 +239,13 @@ struct Agg {
               e = __ldg(p.scores + size_t(k) * p.H + hd);
             }
           }
-          const float cmax = warp_max(e);
+          const float cmax = warp_max_redux(e);
           const float m_old = __shfl_sync(kFull, m_reg, hd);
           const float m_new = fmaxf(m_old, cmax);
           const float pr = valid ? expf(e - m_new) : 0.f;
-          const float ps = warp_sum(pr);
-          const float sc = expf(m_old - m_new);  // 0 on the first chunk (m_old = -inf)
           if (lane == hd) {
-            s_reg = s_reg * sc + ps;
+            sc_reg = expf(m_old - m_new);  // 0 on the first chunk (m_old = -inf)
             m_reg = m_new;
-            sc_reg = sc;
           }
           rescale |= (cb != eb) && (m_new != m_old);
           s_p[lane * p.HS + hd] = pr;
@@ -216,6 +254,7 @@ struct Agg {
 #pragma unroll
           for (int v = 0; v < NV; ++v) {
             const float sc = __shfl_sync(kFull, sc_reg, hv[v]);
+            s_acc[v] *= sc;
 #pragma unroll
             for (int e = 0; e < VEC; ++e) acc[v][e] *= sc;
           }
@@ -245,6 +284,7 @@ struct Agg {
 #pragma unroll
           for (int v = 0; v < NV; ++v) {
             const float a = s_p[(j + u * G) * p.HS + hv[v]];
+            s_acc[v] += a;
 #pragma unroll
             for (int e = 0; e < VEC; ++e) acc[v][e] = fmaf(a, hvv[u][v][e], acc[v][e]);
           }
@@ -253,10 +293,11 @@ struct Agg {
         const char* r = hbase + size_t(s_col[j]) * ldh_b;
 #pragma unroll
         for (int v = 0; v < NV; ++v) {
+          const float a = s_p[j * p.HS + hv[v]];
+          s_acc[v] += a;
           if (!vok[v]) continue;
           float x[VEC];
           VecLoad<TH, VEC>::run(r + voff[v], x);
-          const float a = s_p[j * p.HS + hv[v]];
 #pragma unroll
           for (int e = 0; e < VEC; ++e) acc[v][e] = fmaf(a, x[e], acc[v][e]);
         }
@@ -265,29 +306,65 @@ struct Agg {
     }
   }
 
-  static __device__ __forceinline__ void group_reduce(float (&acc)[NV][VEC]) {
+  static __device__ __forceinline__ void group_reduce(float (&acc)[NV][VEC], float (&s_acc)[NV]) {
 #pragma unroll
     for (int o = LPG; o < 32; o <<= 1)
 #pragma unroll
-      for (int v = 0; v < NV; ++v)
+      for (int v = 0; v < NV; ++v) {
+        s_acc[v] += __shfl_xor_sync(kFull, s_acc[v], o);
 #pragma unroll
         for (int e = 0; e < VEC; ++e) acc[v][e] += __shfl_xor_sync(kFull, acc[v][e], o);
+      }
   }
 
-  // Writes the group-0 lanes' features (divided by den per head) into s_row.
+  // Writes the group-0 lanes' features, scaled by inv[v], into s_row.
   static __device__ __forceinline__ void spill(const AggParams& p, const float (&acc)[NV][VEC],
-                                               float* s_row, const int (&hv)[NV], float den_reg,
-                                               bool divide, int lane) {
-    float den[NV];
-#pragma unroll
-    for (int v = 0; v < NV; ++v) den[v] = __shfl_sync(kFull, den_reg, hv[v]);
+                                               const float (&inv)[NV], float* s_row, int lane) {
     if (lane < LPG) {
 #pragma unroll
       for (int v = 0; v < NV; ++v) {
         const int e0 = (v * LPG + lane) * VEC;
 #pragma unroll
         for (int e = 0; e < VEC; ++e)
-          if (e0 + e < p.F) s_row[e0 + e] = divide ? acc[v][e] / den[v] : acc[v][e];
+          if (e0 + e < p.F) s_row[e0 + e] = acc[v][e] * inv[v];
+      }
+    }
+  }
+
+  // Concatenated heads without log_softmax: the epilogue runs in registers
+  // and each lane stores its VEC outputs with one vector store.
+  static __device__ __forceinline__ void store_row(const AggParams& p, int64_t row,
+                                                   const float (&acc)[NV][VEC],
+                                                   const float (&inv)[NV], int lane) {
+    if (lane >= LPG) return;
+    const size_t base = size_t(row) * size_t(p.ldo);
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const int e0 = (v * LPG + lane) * VEC;
+      if (e0 >= p.F) continue;
+      float o[VEC];
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[e] = acc[v][e] * inv[v];
+      if (p.bias) {
+        if constexpr (VEC % 4 == 0) {
+#pragma unroll
+          for (int e = 0; e < VEC; e += 4) {
+            const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + e0 + e));
+            o[e] += b.x; o[e + 1] += b.y; o[e + 2] += b.z; o[e + 3] += b.w;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) o[e] += __ldg(p.bias + e0 + e);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[e] = apply_act(o[e], p.act);
+      if (e0 + VEC <= p.F) {
+        store_vec<VEC>(p.out, p.out_dtype, base + e0, o);
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e)
+          if (e0 + e < p.F) store_val(p.out, p.out_dtype, base + e0 + e, o[e]);
       }
     }
   }
@@ -316,12 +393,14 @@ __global__ void __launch_bounds__(kThreads) agg_kernel(const AggParams p) {
   const bool softmax = p.mode != MODE_GCN;
 
   int hv[NV];
+  bool head_start[NV];  // this lane's vector v begins head hv[v]
   {
     const int lig = lane % LPG;
 #pragma unroll
     for (int v = 0; v < NV; ++v) {
       const int e0 = (v * LPG + lig) * VEC;
       hv[v] = softmax ? min(e0 / p.C, p.H - 1) : 0;
+      head_start[v] = softmax && lane < LPG && e0 < p.F && (e0 % p.C) == 0;
     }
   }
 
@@ -338,19 +417,22 @@ __global__ void __launch_bounds__(kThreads) agg_kernel(const AggParams p) {
     const int len = ee - eb;
     const int sub = ((len + kWarps - 1) / kWarps + 31) & ~31;
     const int wb = min(ee, eb + warp * sub), we = min(ee, wb + sub);
-    float acc[NV][VEC];
+    float acc[NV][VEC], s_acc[NV], one[NV];
 #pragma unroll
-    for (int v = 0; v < NV; ++v)
+    for (int v = 0; v < NV; ++v) {
+      s_acc[v] = 0.f;
+      one[v] = 1.f;
 #pragma unroll
       for (int e = 0; e < VEC; ++e) acc[v][e] = 0.f;
-    float m_reg = -INFINITY, s_reg = 0.f;
-    A::range(p, row, wb, we, acc, m_reg, s_reg, s_col, s_p, hv, lane);
-    A::group_reduce(acc);
-    A::spill(p, acc, s_row, hv, 1.f, false, lane);
-    if (lane < kHMax) {
-      s_wm[warp * kHMax + lane] = m_reg;
-      s_ws[warp * kHMax + lane] = s_reg;
     }
+    float m_reg = -INFINITY;
+    A::range(p, row, wb, we, acc, s_acc, m_reg, s_col, s_p, hv, lane);
+    A::group_reduce(acc, s_acc);
+    A::spill(p, acc, one, s_row, lane);
+    if (lane < kHMax) s_wm[warp * kHMax + lane] = m_reg;
+#pragma unroll
+    for (int v = 0; v < NV; ++v)
+      if (head_start[v]) s_ws[warp * kHMax + hv[v]] = s_acc[v];
     __syncthreads();
     if (softmax && threadIdx.x < p.H) {
       const int hd = threadIdx.x;
@@ -399,23 +481,33 @@ __global__ void __launch_bounds__(kThreads) agg_kernel(const AggParams p) {
       const int eb = max(int64_t(__ldg(p.rowptr + r)), p.e_lo);
       const int ee = min(int64_t(__ldg(p.rowptr + r + 1)), p.e_hi);
       if (ee - eb > p.cta_threshold) continue;
-      float acc[NV][VEC];
+      float acc[NV][VEC], s_acc[NV], inv[NV];
 #pragma unroll
-      for (int v = 0; v < NV; ++v)
+      for (int v = 0; v < NV; ++v) {
+        s_acc[v] = 0.f;
 #pragma unroll
         for (int e = 0; e < VEC; ++e) acc[v][e] = 0.f;
-      float m_reg = -INFINITY, s_reg = 0.f;
-      if (ee > eb) {
-        A::range(p, r, eb, ee, acc, m_reg, s_reg, s_col, s_p, hv, lane);
-        A::group_reduce(acc);
       }
-      A::spill(p, acc, s_row, hv, s_reg + p.eps, softmax && ee > eb, lane);
-      __syncwarp();
-      warp_epilogue(p, r, s_row, lane);
-      __syncwarp();
+      float m_reg = -INFINITY;
+      if (ee > eb) {
+        A::range(p, r, eb, ee, acc, s_acc, m_reg, s_col, s_p, hv, lane);
+        A::group_reduce(acc, s_acc);
+      }
+      const bool divide = softmax && ee > eb;
+#pragma unroll
+      for (int v = 0; v < NV; ++v) inv[v] = divide ? 1.f / (s_acc[v] + p.eps) : 1.f;
+      if (p.fast_epilogue) {
+        A::store_row(p, r, acc, inv, lane);
+      } else {
+        A::spill(p, acc, inv, s_row, lane);
+        __syncwarp();
+        warp_epilogue(p, r, s_row, lane);
+        __syncwarp();
+      }
     }
   }
 }
+
 
 // Combines the partial (max, sum, acc) slots of every split row in slot order.
 __global__ void __launch_bounds__(kThreads) merge_kernel(const AggParams p) {
@@ -481,6 +573,24 @@ KernelFn pick_layout(int lpg, int nv) {
   return nullptr;
 }
 
+// The register epilogue stores VEC outputs per lane with one vector store and
+// reads bias as float4s: it needs concatenated heads, no log_softmax, and
+// out / ldo / bias aligned for those accesses.
+bool fast_epilogue_ok(const AggParams& p, int vec) {
+  if (!p.concat || p.log_softmax) return false;
+  const uintptr_t o = reinterpret_cast<uintptr_t>(p.out);
+  const size_t osz = p.out_dtype == GNNC_BF16 ? 2 : 4;
+  const size_t vbytes = osz * size_t(vec);
+  const size_t need = vbytes >= 16 ? 16 : vbytes;  // store width per instruction
+  if (vec > 1 && (o % need != 0 || (size_t(p.ldo) * osz) % need != 0)) return false;
+  if (vec % 4 == 0 && p.bias && reinterpret_cast<uintptr_t>(p.bias) % 16 != 0) return false;
+  return true;
+}
+
+// Softmax probabilities are staged as s_p[edge * HS + head]; an odd stride
+// keeps the per-lane stores and the per-head loads free of bank conflicts.
+int head_stride(int mode, int H) { return mode == MODE_GCN ? 1 : (H | 1); }
+
 size_t agg_smem_bytes(int F_pad, int HS) {
   return sizeof(float) * (size_t(kWarps) * 32 + size_t(kWarps) * 32 * HS +
                           size_t(kWarps) * F_pad + 2 * kWarps * kHMax + F_pad + 2 * kHMax);
@@ -534,7 +644,8 @@ int run_aggregate(gnnc_ctx_t* ctx, const Launch& L, AggParams p) {
   if (!fn) return gnnc::set_error(ctx, GNNC_ERR_UNSUPPORTED, "no kernel for layout");
 
   p.F_pad = int(gnnc::align_up(size_t(lpg * vec * nv), 4));
-  p.HS = p.mode == MODE_GCN ? 1 : p.H;
+  p.HS = head_stride(p.mode, p.H);
+  p.fast_epilogue = fast_epilogue_ok(p, vec);
   p.part_stride = part_stride_floats(p.F_pad);
   p.cta_items = plan->cta_items;
   p.n_cta_items = plan->n_cta_items;
@@ -907,7 +1018,8 @@ extern "C" int gnnc_gat_aggregate_noalloc(gnnc_ctx_t* ctx, const gnnc_plan_t* pl
     fn = vec == 4 ? pick_layout<float, 4>(lpg, nv) : pick_layout<float, 1>(lpg, nv);
   if (!fn) return gnnc::set_error(ctx, GNNC_ERR_UNSUPPORTED, "no kernel for layout");
   p.F_pad = int(gnnc::align_up(size_t(lpg * vec * nv), 4));
-  p.HS = p.H;
+  p.HS = head_stride(p.mode, p.H);
+  p.fast_epilogue = fast_epilogue_ok(p, vec);
   p.part_stride = part_stride_floats(p.F_pad);
   p.cta_items = plan->cta_items;
   p.n_cta_items = plan->n_cta_items;
