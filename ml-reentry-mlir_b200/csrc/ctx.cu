@@ -116,8 +116,16 @@ int gnnc_synchronize(gnnc_ctx_t* ctx) {
   GNNC_CUDA_TRY(ctx, cudaGetLastError());
   // Word 2 is set by the aggregation kernels when they meet a column index
   // outside the feature table (the edge is skipped, never dereferenced).
-  int flag = 0;
-  GNNC_CUDA_TRY(ctx, cudaMemcpy(&flag, ctx->dev_words + 2, sizeof(int), cudaMemcpyDeviceToHost));
+  // Word 3 is set by a tensor-core projection whose bounded wait gave up.
+  int words[2] = {0, 0};
+  GNNC_CUDA_TRY(ctx, cudaMemcpy(words, ctx->dev_words + 2, sizeof(words), cudaMemcpyDeviceToHost));
+  const int flag = words[0];
+  if (words[1]) {
+    GNNC_CUDA_TRY(ctx, cudaMemset(ctx->dev_words + 3, 0, sizeof(int)));
+    return gnnc::set_error(ctx, GNNC_ERR_TIMEOUT,
+                           "a tensor-core projection gave up waiting on its pipeline; "
+                           "its output is incomplete");
+  }
   if (flag) {
     GNNC_CUDA_TRY(ctx, cudaMemset(ctx->dev_words + 2, 0, sizeof(int)));
     return gnnc::set_error(ctx, GNNC_ERR_BOUNDS,
