@@ -109,9 +109,11 @@ struct VecLoad<__nv_bfloat16, 1> {
   }
 };
 
+// ELU as exp(x) - 1 for x <= 0 with the fast exponential (absolute error
+// ~1e-7 on [-inf, 0], far inside the fp32 parity tolerance).
 __device__ __forceinline__ float apply_act(float v, int act) {
   if (act == GNNC_ACT_RELU) return fmaxf(v, 0.f);
-  if (act == GNNC_ACT_ELU) return v > 0.f ? v : expm1f(v);
+  if (act == GNNC_ACT_ELU) return v > 0.f ? v : __expf(v) - 1.f;
   return v;
 }
 
@@ -214,6 +216,9 @@ struct Agg {
       vok[v] = e0 < p.F;
     }
     float sc_reg = 1.f;
+    // a_dst of this row: lane hd holds head hd's value (broadcast per head below).
+    float ad_reg = 0.f;
+    if (p.mode == MODE_GAT && lane < p.H) ad_reg = __ldg(p.adst + size_t(row) * p.H + lane);
     for (int cb = eb; cb < ee; cb += 32) {
       const int k = cb + lane;
       bool valid = k < ee;
@@ -228,23 +233,27 @@ struct Agg {
         s_p[lane] = valid ? __ldg(p.w + k) : 0.f;
       } else {
         bool rescale = false;
+        const float* as = p.asrc + size_t(src) * p.H;
+        const float* sc_row = p.scores + size_t(k) * p.H;
         for (int hd = 0; hd < p.H; ++hd) {
+          const float ad = __shfl_sync(kFull, ad_reg, hd);
           float e = -INFINITY;
           if (valid) {
             if (p.mode == MODE_GAT) {
-              const float x = __ldg(p.asrc + size_t(src) * p.H + hd) +
-                              __ldg(p.adst + size_t(row) * p.H + hd);
+              const float x = __ldg(as + hd) + ad;
               e = x > 0.f ? x : x * p.slope;
             } else {
-              e = __ldg(p.scores + size_t(k) * p.H + hd);
+              e = __ldg(sc_row + hd);
             }
           }
           const float cmax = warp_max_redux(e);
           const float m_old = __shfl_sync(kFull, m_reg, hd);
           const float m_new = fmaxf(m_old, cmax);
-          const float pr = valid ? expf(e - m_new) : 0.f;
+          // Fast exponential: relative error ~1e-6 for the arguments here (<= 0).
+          const float pr = valid ? __expf(e - m_new) : 0.f;
+          const float sc = __expf(m_old - m_new);  // 0 on the first chunk (m_old = -inf)
           if (lane == hd) {
-            sc_reg = expf(m_old - m_new);  // 0 on the first chunk (m_old = -inf)
+            sc_reg = sc;
             m_reg = m_new;
           }
           rescale |= (cb != eb) && (m_new != m_old);
@@ -371,7 +380,7 @@ struct Agg {
 };
 
 template <typename TH, int VEC, int LPG, int NV>
-__global__ void __launch_bounds__(kThreads) agg_kernel(const AggParams p) {
+__global__ void __launch_bounds__(kThreads, 4) agg_kernel(const AggParams p) {
   using A = Agg<TH, VEC, LPG, NV>;
   extern __shared__ float smem[];
   const int warp = threadIdx.x >> 5;

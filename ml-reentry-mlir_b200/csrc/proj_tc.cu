@@ -12,9 +12,10 @@
 //     one lane issues tcgen05.mma (M = 128, N = F16, K = 16 per instruction)
 //     and tcgen05.commit to release stages and publish finished tiles.
 //   warps 2-5: epilogue. Warp w reads TMEM lanes 32*(w%4) .. +31 (one tile row
-//     per thread) with tcgen05.ld, converts, stores the row of h and folds the
-//     per-head dot products with att_src / att_dst (sequential over columns:
-//     deterministic).
+//     per thread) with tcgen05.ld, folds the per-head dot products with
+//     att_src / att_dst (sequential over columns: deterministic), converts the
+//     row into a padded shared-memory staging tile, releases the accumulator,
+//     then writes its 32 rows to h with one coalesced 512-byte store per row.
 // The two accumulators let the MMAs of tile i+1 run under the epilogue of
 // tile i. Every mbarrier wait is bounded by %globaltimer; a wait that gives up
 // raises an abort flag the other roles see, records GNNC_ERR_TIMEOUT in the
@@ -30,13 +31,20 @@ namespace {
 
 constexpr int kBM = 128;  // tile rows = MMA M
 constexpr int kBK = 64;   // k-block: 64 bf16 = one 128-byte swizzle row
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 constexpr int kEpiWarps = 4;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccStride = 256;  // TMEM columns per accumulator buffer
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s per wait
 constexpr int kMaxF = 256;
+// Per epilogue warp: 32 output rows of up to 512 bytes, padded by 16 bytes so
+// the per-thread row writes hit distinct banks.
+constexpr int kStageRowBytes = 512 + 16;
+// Bytes reserved for the 2*kStages + 5 mbarriers (a multiple of 16).
+constexpr int kBarrierBytes = ((2 * kStages + 5) * 8 + 15) / 16 * 16;
+static_assert(kStageRowBytes % 16 == 0 && kBarrierBytes % 16 == 0, "16-byte aligned regions");
+static_assert((2 * kMaxF * 4) % 16 == 0, "staging must start 16-byte aligned");
 
 struct TcParams {
   int N, K, F, N16, nkb, n_tiles;
@@ -75,14 +83,17 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
 }
 
+// One try_wait. The suspend hint lets the hardware park the thread until the
+// phase completes (or ~10 ms pass) instead of spinning on issue slots that the
+// epilogue warps sharing the scheduler need.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}\n"
       : "=r"(ok)
-      : "r"(smem_u32(b)), "r"(parity)
+      : "r"(smem_u32(b)), "r"(parity), "r"(10000000u)
       : "memory");
   return ok != 0;
 }
@@ -92,14 +103,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort,
                                           bool watch_abort = true) {
   const unsigned long long t0 = now_ns();
-  for (uint32_t i = 0;; ++i) {
+  for (;;) {
     if (mbar_try_wait(b, parity)) return true;
-    if ((i & 63) == 63) {
-      if (watch_abort && *abort) return false;
-      if (now_ns() - t0 > kWaitNs) {
-        *abort = 1;
-        return false;
-      }
+    if (watch_abort && *abort) return false;
+    if (now_ns() - t0 > kWaitNs) {
+      *abort = 1;
+      return false;
     }
   }
 }
@@ -147,6 +156,25 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+// 32 lanes x 32 consecutive 32-bit TMEM columns -> 32 registers per thread
+// (no wait: the caller batches loads before one tcgen05.wait::ld).
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 // 32 lanes x 16 consecutive 32-bit TMEM columns -> 16 registers per thread.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
@@ -179,15 +207,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int a_bytes = kBM * kBK * 2;
   const int b_bytes = p.N16 * kBK * 2;
   const int stage_bytes = a_bytes + b_bytes;  // multiple of 1024 (N16 % 16 == 0)
+  // Carve-up (offsets from the 1024-byte aligned base; every region starts on
+  // a multiple of 16 bytes whatever kStages is):
+  //   [stages][kBarrierBytes: mbarriers][16: TMEM address, abort flag]
+  //   [2*kMaxF floats: att_src, att_dst][kEpiWarps*32 rows: output staging]
   unsigned char* stages = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * stage_bytes);
+  unsigned char* bar_base = smem + kStages * stage_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(bar_base);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_base + kBarrierBytes);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* s_att = reinterpret_cast<float*>(tmem_slot + 4);  // [2][kMaxF]
+  float* s_att = reinterpret_cast<float*>(bar_base + kBarrierBytes + 16);  // [2][kMaxF]
+  unsigned char* s_stage = reinterpret_cast<unsigned char*>(s_att + 2 * kMaxF);  // [kEpiWarps][32][kStageRowBytes]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -287,7 +321,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Epilogue: one tile row per thread.
     const int q = warp & 3;
     const int rloc = q * 32 + lane;
-    const int nch = p.N16 / 16;
+    const int esize = p.h_bf16 ? 2 : 4;
+    const int pass_cols = 512 / esize;  // columns staged per pass
+    unsigned char* stage = s_stage + (warp - 2) * 32 * kStageRowBytes;
     int t_iter = 0;
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++t_iter) {
       const int b = t_iter & 1;
@@ -298,62 +334,97 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t taddr = tmem + (uint32_t(q * 32) << 16) + uint32_t(b) * kAccStride;
       float run_s = 0.f, run_d = 0.f;
       int cur = 0;
-      for (int c = 0; c < nch; ++c) {
-        uint32_t r[16];
-        tmem_ld16(taddr + uint32_t(c * 16), r);
-        float v[16];
+      for (int p0 = 0; p0 < p.N16; p0 += pass_cols) {
+        const int p1 = min(p.N16, p0 + pass_cols);
+        int col0 = p0;
+        for (; col0 < p1; col0 += 64) {
+          // 64 columns per tcgen05.wait::ld when they fit, else 16 at a time.
+          const int width = (col0 + 64 <= p1) ? 64 : 16;
+          uint32_t r[64];
+          if (width == 64) {
+            tmem_ld32_async(taddr + uint32_t(col0), r);
+            tmem_ld32_async(taddr + uint32_t(col0 + 32), r + 32);
+            tmem_wait_ld();
+          } else {
+            uint32_t r16[16];
+            tmem_ld16(taddr + uint32_t(col0), r16);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(r[e]);
-        const int col0 = c * 16;
-        if (live) {
-          if (p.h_bf16) {
-            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.h) + size_t(row) * p.ldh + col0;
-            if (col0 + 16 <= p.F) {
-              uint4* o4 = reinterpret_cast<uint4*>(o);
+            for (int e = 0; e < 16; ++e) r[e] = r16[e];
+          }
+          for (int sub = 0; sub < width; sub += 16) {
+            const int c0 = col0 + sub;
+            float v[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(r[sub + e]);
+            if (att && live) {
+              // Heads are contiguous column ranges; a 16-column chunk lies in
+              // one head (C % 16 == 0 or H == 1), so the sums run per head.
+              const int hd = p.H == 1 ? 0 : c0 / p.C;
+              if (hd != cur) {
+                p.asrc[size_t(row) * p.H + cur] = run_s;
+                p.adst[size_t(row) * p.H + cur] = run_d;
+                run_s = run_d = 0.f;
+                cur = hd;
+              }
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                const float ws = c0 + e < p.F ? s_att[c0 + e] : 0.f;
+                const float wd = c0 + e < p.F ? s_att[kMaxF + c0 + e] : 0.f;
+                run_s = fmaf(v[e], ws, run_s);
+                run_d = fmaf(v[e], wd, run_d);
+              }
+            }
+            unsigned char* srow = stage + lane * kStageRowBytes + (c0 - p0) * esize;
+            if (p.h_bf16) {
+              uint4* o4 = reinterpret_cast<uint4*>(srow);
               o4[0] = make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]),
                                  pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
               o4[1] = make_uint4(pack_bf16(v[8], v[9]), pack_bf16(v[10], v[11]),
                                  pack_bf16(v[12], v[13]), pack_bf16(v[14], v[15]));
             } else {
-              for (int e = 0; e < 16 && col0 + e < p.F; ++e) o[e] = __float2bfloat16_rn(v[e]);
-            }
-          } else {
-            float* o = reinterpret_cast<float*>(p.h) + size_t(row) * p.ldh + col0;
-            if (col0 + 16 <= p.F) {
+              float4* o4 = reinterpret_cast<float4*>(srow);
 #pragma unroll
-              for (int e = 0; e < 16; e += 4)
-                *reinterpret_cast<float4*>(o + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-            } else {
-              for (int e = 0; e < 16 && col0 + e < p.F; ++e) o[e] = v[e];
+              for (int e = 0; e < 4; ++e)
+                o4[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
             }
           }
-          if (att) {
-            // Heads are contiguous column ranges; a 16-column chunk lies in
-            // one head (C % 16 == 0 or H == 1), so the sums run per head.
-            const int hd = p.H == 1 ? 0 : col0 / p.C;
-            if (hd != cur) {
-              p.asrc[size_t(row) * p.H + cur] = run_s;
-              p.adst[size_t(row) * p.H + cur] = run_d;
-              run_s = run_d = 0.f;
-              cur = hd;
-            }
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              if (col0 + e < p.F) {
-                run_s = fmaf(v[e], s_att[col0 + e], run_s);
-                run_d = fmaf(v[e], s_att[kMaxF + col0 + e], run_d);
-              }
+          if (width == 16) col0 -= 48;  // advance by 16 for the tail chunks
+        }
+        if (p1 >= p.N16) {
+          // Accumulator fully read: hand it back to the MMA warp.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[b]);
+        }
+        __syncwarp();
+        // Coalesced write-out of this warp's 32 rows, columns [p0, min(F, p1)).
+        const int cols = min(p.F, p1) - p0;
+        if (cols > 0) {
+          const int bytes = cols * esize;
+          const int n16 = bytes / 16;
+#pragma unroll 4
+          for (int rr = 0; rr < 32; ++rr) {
+            const int64_t grow = int64_t(tile) * kBM + q * 32 + rr;
+            if (grow >= p.N) continue;
+            unsigned char* g = reinterpret_cast<unsigned char*>(p.h) +
+                               (size_t(grow) * size_t(p.ldh) + size_t(p0)) * esize;
+            const unsigned char* sr = stage + rr * kStageRowBytes;
+            for (int j = lane; j < n16; j += 32)
+              *reinterpret_cast<uint4*>(g + j * 16) = *reinterpret_cast<const uint4*>(sr + j * 16);
+            for (int j = n16 * 16 + lane * esize; j < bytes; j += 32 * esize) {
+              if (esize == 2)
+                *reinterpret_cast<uint16_t*>(g + j) = *reinterpret_cast<const uint16_t*>(sr + j);
+              else
+                *reinterpret_cast<uint32_t*>(g + j) = *reinterpret_cast<const uint32_t*>(sr + j);
             }
           }
         }
+        __syncwarp();
       }
       if (att && live) {
         p.asrc[size_t(row) * p.H + cur] = run_s;
         p.adst[size_t(row) * p.H + cur] = run_d;
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[b]);
     }
   }
 
@@ -449,7 +520,10 @@ int proj_tc_try(gnnc_ctx_t* ctx, const void* x, int64_t ldx, const void* w, int6
   p.err = ctx->dev_words + 3;
 
   const size_t stage_bytes = size_t(kBM) * kBK * 2 + size_t(N16) * kBK * 2;
-  size_t smem = 1024 + kStages * stage_bytes + 256 + 2 * kMaxF * sizeof(float);
+  static_assert((kBM * kBK * 2) % 1024 == 0, "stage base alignment");
+  if (stage_bytes % 1024 != 0) return kProjTcDeclined;  // keeps every stage 1024-byte aligned
+  size_t smem = 1024 + kStages * stage_bytes + kBarrierBytes + 16 + 2 * kMaxF * sizeof(float) +
+                size_t(kEpiWarps) * 32 * kStageRowBytes;
   // At least 120 KB, so two CTAs never share an SM (each takes all 512 TMEM columns).
   if (smem < 120 * 1024) smem = 120 * 1024;
   GNNC_CUDA_TRY(ctx, cudaFuncSetAttribute(proj_tc_kernel,

@@ -17,6 +17,7 @@ activation and the final log_softmax fused into its epilogue.
 from __future__ import annotations
 
 import operator
+import sys
 from dataclasses import dataclass, field
 
 import torch
@@ -312,6 +313,32 @@ def to_device_features(x: torch.Tensor, dtype: torch.dtype, device) -> torch.Ten
     return out
 
 
+class _PinnedResults:
+    """Page-locked host buffers for results, recycled across calls.
+
+    Allocating page-locked memory costs about as much as the transfer it
+    speeds up (hundreds of ms per GB), so results for host inputs are written
+    into buffers kept here. A buffer is handed out again only when nothing but
+    this pool references it (views and numpy arrays of a result keep it
+    referenced), so a result the caller still holds is never overwritten.
+    """
+
+    def __init__(self, max_buffers: int = 4) -> None:
+        self.max_buffers = max_buffers
+        self.pool: dict[tuple, list[torch.Tensor]] = {}
+
+    def take(self, shape: tuple, dtype: torch.dtype) -> torch.Tensor:
+        bufs = self.pool.setdefault((tuple(shape), dtype), [])
+        for buf in bufs:
+            # references: the pool list, this loop variable, getrefcount's argument
+            if sys.getrefcount(buf) <= 3:
+                return buf
+        buf = torch.empty(tuple(shape), dtype=dtype, pin_memory=True)
+        if len(bufs) < self.max_buffers:
+            bufs.append(buf)
+        return buf
+
+
 class B200Executable:
     """A lowered model bound to one CUDA device. Call with the forward inputs."""
 
@@ -332,12 +359,24 @@ class B200Executable:
             bias = None if layer.bias is None else layer.bias.to(self.device, torch.float32)
             self._weights.append((w, asrc, adst, bias))
         self._graphs: dict[tuple, tuple[object, DeviceGraph]] = {}
+        self._results = _PinnedResults()
 
     def __str__(self) -> str:
         return f"b200.executable(device={self.device})\n{self.program}"
 
-    # Graphs are cached per (tensor identity, version, layer graph mode); the
-    # cache holds the source tensor so its id cannot be reused meanwhile.
+    # Graphs are cached per (storage, shape, strides, version counter, layer
+    # graph mode). detach() and views share the storage and the version counter,
+    # so the same user tensor hits the cache on every call, while an in-place
+    # update (version bump) rebuilds it. The cache holds the tensor, keeping its
+    # storage (and address) alive.
+    @staticmethod
+    def _graph_key(graph: torch.Tensor) -> tuple:
+        if graph.layout == torch.sparse_csr:
+            parts = (graph.crow_indices(), graph.col_indices(), graph.values())
+            return tuple((t.device, t.data_ptr(), tuple(t.shape), t._version) for t in parts)
+        return (graph.device, graph.data_ptr(), tuple(graph.shape), tuple(graph.stride()),
+                graph.dtype, graph._version)
+
     def _graph_for(self, graph: torch.Tensor, num_nodes: int, layer: LayerOp) -> DeviceGraph:
         if graph.layout == torch.sparse_csr:
             if layer.kind != "gcn" or layer.normalize:
@@ -352,9 +391,9 @@ class B200Executable:
                 mode = ("coo", layer.add_self_loops, False, False)
         else:
             raise NotImplementedError(f"unsupported graph layout {graph.layout}")
-        key = (id(graph), graph._version, *mode)
+        key = (self._graph_key(graph), num_nodes, *mode)
         hit = self._graphs.get(key)
-        if hit is not None and hit[0] is graph:
+        if hit is not None:
             return hit[1]
         if mode[0] == "csr":
             g = graph_from_csr(graph, self.device)
@@ -400,9 +439,8 @@ class B200Executable:
         x, graph = inputs
         out = self.run_device(x, graph)
         if not x.is_cuda:
-            # Pinned host result: the DMA runs at full PCIe rate and torch's
-            # pinned caching allocator recycles the buffer across calls.
-            host = torch.empty(tuple(out.shape), dtype=out.dtype, pin_memory=True)
+            # Page-locked result buffer: the copy runs as one DMA at full rate.
+            host = self._results.take(tuple(out.shape), out.dtype)
             host.copy_(out, non_blocking=True)
             torch.cuda.current_stream(self.device).synchronize()
             return [host]

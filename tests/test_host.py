@@ -117,3 +117,43 @@ def test_config_model_power_law_tail():
     assert ei.size(1) == 200000
     deg = np.bincount(ei[1].numpy(), minlength=20000)
     assert deg.max() > 20 * deg.mean()  # heavy tail
+
+
+def test_pinned_result_pool_never_hands_out_a_held_buffer(monkeypatch):
+    """Result buffers are recycled only when the caller dropped every reference."""
+    from gnnc.b200 import program
+
+    made = []
+
+    def fake_empty(shape, dtype, pin_memory):
+        t = torch.zeros(shape, dtype=dtype)
+        made.append(id(t))
+        return t
+
+    monkeypatch.setattr(program.torch, "empty", fake_empty)
+    pool = program._PinnedResults()
+    a = pool.take((4, 2), torch.float32)
+    b = pool.take((4, 2), torch.float32)
+    assert a is not b  # a is still held
+    view = b[1:]
+    del b
+    c = pool.take((4, 2), torch.float32)
+    assert c is not view._base  # a view keeps its buffer busy
+    del a
+    d = pool.take((4, 2), torch.float32)
+    assert id(d) == made[0]  # a was dropped: recycled
+    assert len(made) == 3
+
+
+def test_graph_cache_key_survives_detach_and_tracks_updates():
+    """run_jit hands the executable detached tensors; the graph cache must still
+    hit for the same storage and miss after an in-place update."""
+    from gnnc.b200.program import B200Executable
+
+    ei = torch.randint(0, 10, (2, 30))
+    k1 = B200Executable._graph_key(ei)
+    assert B200Executable._graph_key(ei.detach()) == k1
+    ei.add_(0)  # in-place: bumps the version counter
+    assert B200Executable._graph_key(ei.detach()) != k1
+    other = ei.clone()
+    assert B200Executable._graph_key(other) != B200Executable._graph_key(ei)
