@@ -224,6 +224,7 @@ def broadcast_workload(rank, world, device, scale=1.0):
 
 
 def run_b200(args) -> None:
+    from gnnc.b200 import partition as P
     from gnnc.b200 import runtime as rt
     from gnnc.b200.program import to_device_features
 
@@ -235,19 +236,17 @@ def run_b200(args) -> None:
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
 
     cfg, ei_host, x_host, ei_d, x_d = broadcast_workload(rank, world, device, args.scale)
     N = x_d.size(0)
     rowptr, col, _ = rt.csr_from_coo(ei_d, N, self_loops=True, dedupe=False)
     del ei_d
     E = col.numel()
-    R = (N + world - 1) // world
-    r0, r1 = rank * R, min(N, (rank + 1) * R)
-    n_loc = r1 - r0
-    e0, e1 = (int(v) for v in rowptr[[r0, r1]].tolist())
-    rowptr_l = (rowptr[r0 : r1 + 1] - e0).contiguous()
-    col_l = col[e0:e1].contiguous()
+    rr = P.row_range(N, world, rank)
+    r0, n_loc, R = rr.begin, rr.count, rr.rows_per_rank
+    rowptr_l, col_l = P.local_csr(rowptr, col, rr)
+    e_loc = col_l.numel()
     del rowptr, col
     plan = rt.Plan(rowptr_l, cta_threshold=args.cta_threshold, split_threshold=args.split_threshold)
     info = plan.info()
@@ -258,21 +257,20 @@ def run_b200(args) -> None:
     att_s = conv.att_src.detach().reshape(-1).to(device)
     att_d = conv.att_dst.detach().reshape(-1).to(device)
     bias = conv.bias.detach().to(device)
-    X_l = to_device_features(x_d[r0:r1], torch.bfloat16, device)
+    X_l = to_device_features(x_d[r0 : r0 + n_loc], torch.bfloat16, device)
     del x_d
-    h_full = torch.empty((world * R, F), dtype=torch.bfloat16, device=device)
-    a_full = torch.empty((world * R, HEADS), dtype=torch.float32, device=device)
+    h_full = P.gathered_table(rr, F, torch.bfloat16, device)
+    a_full = P.gathered_table(rr, HEADS, torch.float32, device)
     adst_l = torch.empty((n_loc, HEADS), dtype=torch.float32, device=device)
     out_l = rt.empty_rows(n_loc, F, torch.bfloat16, device)
-    h_mine = h_full[r0 : r0 + n_loc]
-    a_mine = a_full[r0 : r0 + n_loc]
+    h_mine = P.my_rows(h_full, rr)
+    a_mine = P.my_rows(a_full, rr)
 
     def project():
         rt.proj(X_l, W, att_src=att_s, att_dst=att_d, heads=HEADS, out_dtype=torch.bfloat16,
                 out=h_mine, asrc_out=a_mine, adst_out=adst_l)
-        if world > 1:
-            dist.all_gather_into_tensor(h_full, h_full[r0 : r0 + R])
-            dist.all_gather_into_tensor(a_full, a_full[r0 : r0 + R])
+        P.all_gather_rows(h_full, rr)
+        P.all_gather_rows(a_full, rr)
 
     def aggregate():
         rt.gat_aggregate(plan, rowptr_l, col_l, h_full[:N], a_full[:N], adst_l, heads=HEADS,
@@ -310,8 +308,8 @@ def run_b200(args) -> None:
     total_ms = t_start.elapsed_time(t_end)
     agg_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
     proj_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
-    loc_bytes = algorithmic_bytes(e1 - e0, n_loc)
-    stats = torch.tensor([total_ms, agg_ms, proj_ms, float(loc_bytes), float(e1 - e0)],
+    loc_bytes = algorithmic_bytes(e_loc, n_loc)
+    stats = torch.tensor([total_ms, agg_ms, proj_ms, float(loc_bytes), float(e_loc)],
                          dtype=torch.float64, device=device)
     if world > 1:
         gathered = [torch.empty_like(stats) for _ in range(world)]
