@@ -4,18 +4,19 @@
 // the epilogue from the fp32 accumulator.
 //
 // One persistent CTA per SM walks 128-row tiles of x. Warp roles:
-//   warp 0 (one lane): TMA producer. Each pipeline stage holds a 128 x 64
-//     k-block of x and the matching F16 x 64 k-block of w, both in the
-//     128-byte-swizzled K-major layout, loaded with cp.async.bulk.tensor into a
-//     4-stage ring guarded by mbarriers (no multicast).
-//   warp 1: allocates 512 TMEM columns (two 128 x 256 fp32 accumulators), and
-//     one lane issues tcgen05.mma (M = 128, N = F16, K = 16 per instruction)
-//     and tcgen05.commit to release stages and publish finished tiles.
-//   warps 2-5: epilogue. Warp w reads TMEM lanes 32*(w%4) .. +31 (one tile row
-//     per thread) with tcgen05.ld, folds the per-head dot products with
-//     att_src / att_dst (sequential over columns: deterministic), converts the
-//     row into a padded shared-memory staging tile, releases the accumulator,
-//     then writes its 32 rows to h with one coalesced 512-byte store per row.
+//   warp 0 (one lane): TMA producer (cp.async.bulk.tensor, no multicast). When
+//     all k-blocks of w fit in 64 KB they are loaded once and stay resident,
+//     and the ring of stages carries only 128 x 64 k-blocks of x; otherwise
+//     each stage carries the x k-block and the matching w k-block. Operands are
+//     in the 128-byte-swizzled K-major layout.
+//   warp 1: allocates 512 TMEM columns (two 128 x 256 fp32 accumulators); one
+//     lane issues tcgen05.mma (M = 128, N = F16, K = 16 per instruction) and
+//     tcgen05.commit to release stages and publish finished tiles.
+//   warps 2-5: attention epilogue. Warp w reads TMEM lanes 32*(w%4) .. +31
+//     (one tile row per thread) and folds the per-head dot products with
+//     att_src / att_dst (fixed summation order: deterministic).
+//   warps 6-9: output epilogue. Same rows; convert, stage in padded shared
+//     memory, then one coalesced store per output row.
 // The two accumulators let the MMAs of tile i+1 run under the epilogue of
 // tile i. Every mbarrier wait is bounded by %globaltimer; a wait that gives up
 // raises an abort flag the other roles see, records GNNC_ERR_TIMEOUT in the
@@ -31,23 +32,30 @@ namespace {
 
 constexpr int kBM = 128;  // tile rows = MMA M
 constexpr int kBK = 64;   // k-block: 64 bf16 = one 128-byte swizzle row
-constexpr int kStages = 3;
-constexpr int kEpiWarps = 4;
+constexpr int kStagesResident = 5;  // x-only stages when w stays resident
+constexpr int kStagesStream = 3;    // x + w stages otherwise
+constexpr int kMaxStages = 5;
+constexpr int kAttWarps = 4;
+constexpr int kOutWarps = 4;
+constexpr int kEpiWarps = kAttWarps + kOutWarps;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccStride = 256;  // TMEM columns per accumulator buffer
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s per wait
 constexpr int kMaxF = 256;
-// Per epilogue warp: 32 output rows of up to 512 bytes, padded by 16 bytes so
-// the per-thread row writes hit distinct banks.
+constexpr int kResidentWBytes = 64 * 1024;
+// Per output warp: 32 rows of up to 512 bytes, padded by 16 bytes so the
+// per-thread row writes hit distinct banks.
 constexpr int kStageRowBytes = 512 + 16;
-// Bytes reserved for the 2*kStages + 5 mbarriers (a multiple of 16).
-constexpr int kBarrierBytes = ((2 * kStages + 5) * 8 + 15) / 16 * 16;
+// Bytes reserved for the 2*kMaxStages + 6 mbarriers (a multiple of 16).
+constexpr int kBarrierBytes = ((2 * kMaxStages + 6) * 8 + 15) / 16 * 16;
 static_assert(kStageRowBytes % 16 == 0 && kBarrierBytes % 16 == 0, "16-byte aligned regions");
 static_assert((2 * kMaxF * 4) % 16 == 0, "staging must start 16-byte aligned");
 
 struct TcParams {
   int N, K, F, N16, nkb, n_tiles;
+  int w_resident;  // all w k-blocks live in shared memory for the whole kernel
+  int stages;
   int H, C;
   const float* att_src;
   const float* att_dst;
@@ -204,31 +212,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int a_bytes = kBM * kBK * 2;
-  const int b_bytes = p.N16 * kBK * 2;
-  const int stage_bytes = a_bytes + b_bytes;  // multiple of 1024 (N16 % 16 == 0)
+  const int a_bytes = kBM * kBK * 2;                // 16 KB
+  const int b_bytes = p.N16 * kBK * 2;              // one w k-block
+  const int stage_bytes = p.w_resident ? a_bytes : a_bytes + b_bytes;  // multiple of 1024
+  const int S = p.stages;
   // Carve-up (offsets from the 1024-byte aligned base; every region starts on
-  // a multiple of 16 bytes whatever kStages is):
-  //   [stages][kBarrierBytes: mbarriers][16: TMEM address, abort flag]
-  //   [2*kMaxF floats: att_src, att_dst][kEpiWarps*32 rows: output staging]
-  unsigned char* stages = smem;
-  unsigned char* bar_base = smem + kStages * stage_bytes;
+  // a multiple of 16 bytes):
+  //   [resident w: nkb * b_bytes][S stages][kBarrierBytes: mbarriers]
+  //   [16: TMEM address, abort flag][2*kMaxF floats: att_src, att_dst]
+  //   [kOutWarps * 32 rows: output staging]
+  unsigned char* w_res = smem;
+  unsigned char* stages = smem + (p.w_resident ? p.nkb * b_bytes : 0);
+  unsigned char* bar_base = stages + S * stage_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(bar_base);
-  uint64_t* empty = full + kStages;
-  uint64_t* tfull = empty + kStages;
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* tfull = empty + kMaxStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
+  uint64_t* wfull = drain + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_base + kBarrierBytes);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* s_att = reinterpret_cast<float*>(bar_base + kBarrierBytes + 16);  // [2][kMaxF]
-  unsigned char* s_stage = reinterpret_cast<unsigned char*>(s_att + 2 * kMaxF);  // [kEpiWarps][32][kStageRowBytes]
+  unsigned char* s_stage = reinterpret_cast<unsigned char*>(s_att + 2 * kMaxF);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const bool att = p.att_src != nullptr;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -237,14 +249,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[b], kEpiWarps);
     }
     mbar_init(drain, 1);
+    mbar_init(wfull, 1);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (att)
-    for (int i = threadIdx.x; i < p.F; i += kThreads) {
-      s_att[i] = p.att_src[i];
-      s_att[kMaxF + i] = p.att_dst[i];
-    }
+  // Attention vectors, zero beyond F so the epilogue needs no column test.
+  for (int i = threadIdx.x; i < kMaxF; i += kThreads) {
+    s_att[i] = (att && i < p.F) ? p.att_src[i] : 0.f;
+    s_att[kMaxF + i] = (att && i < p.F) ? p.att_dst[i] : 0.f;
+  }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
@@ -258,12 +271,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
+      if (p.w_resident) {
+        mbar_expect_tx(wfull, uint32_t(p.nkb * b_bytes));
+        for (int kb = 0; kb < p.nkb; ++kb) tma_load_2d(w_res + kb * b_bytes, &map_w, wfull, kb * kBK, 0);
+      }
       int it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.n_tiles; tile += gridDim.x) {
         for (int kb = 0; kb < p.nkb; ++kb) {
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1;
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, abort)) {
             ok = false;
             break;
@@ -271,21 +288,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_expect_tx(&full[s], uint32_t(stage_bytes));
           unsigned char* dst = stages + s * stage_bytes;
           tma_load_2d(dst, &map_x, &full[s], kb * kBK, tile * kBM);
-          tma_load_2d(dst + a_bytes, &map_w, &full[s], kb * kBK, 0);
+          if (!p.w_resident) tma_load_2d(dst + a_bytes, &map_w, &full[s], kb * kBK, 0);
           ++it;
         }
       }
       if (!ok) {
         // Let the copies still in flight land before the CTA goes away.
-        for (int j = it > kStages ? it - kStages : 0; j < it; ++j)
-          mbar_wait(&full[j % kStages], (j / kStages) & 1, abort, false);
+        for (int j = it > S ? it - S : 0; j < it; ++j)
+          mbar_wait(&full[j % S], (j / S) & 1, abort, false);
+        if (p.w_resident) mbar_wait(wfull, 0, abort, false);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16(p.N16);
       int it = 0, t_iter = 0;
-      bool ok = true;
+      bool ok = !p.w_resident || mbar_wait(wfull, 0, abort);
       for (int tile = blockIdx.x; ok && tile < p.n_tiles; tile += gridDim.x, ++t_iter) {
         const int b = t_iter & 1;
         if (!mbar_wait(&tempty[b], ((t_iter >> 1) & 1) ^ 1, abort)) {
@@ -295,15 +313,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d = tmem + uint32_t(b) * kAccStride;
         for (int kb = 0; kb < p.nkb; ++kb) {
-          const int s = it % kStages;
-          if (!mbar_wait(&full[s], (it / kStages) & 1, abort)) {
+          const int s = it % S;
+          if (!mbar_wait(&full[s], (it / S) & 1, abort)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(stages + s * stage_bytes);
+          const uint32_t b_addr =
+              p.w_resident ? smem_u32(w_res + kb * b_bytes) : a_addr + uint32_t(a_bytes);
           const uint64_t adesc = sw128_desc(a_addr);
-          const uint64_t bdesc = sw128_desc(a_addr + uint32_t(a_bytes));
+          const uint64_t bdesc = sw128_desc(b_addr);
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k)
             umma_bf16(d, adesc + uint64_t(2 * k), bdesc + uint64_t(2 * k), idesc,
@@ -317,28 +337,86 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(drain);
       mbar_wait(drain, 0, abort, false);
     }
-  } else {
-    // Epilogue: one tile row per thread.
+  } else if (warp < 2 + kAttWarps) {
+    // Attention epilogue: per-head dot products of each row with att_src / att_dst.
     const int q = warp & 3;
     const int rloc = q * 32 + lane;
-    const int esize = p.h_bf16 ? 2 : 4;
-    const int pass_cols = 512 / esize;  // columns staged per pass
-    unsigned char* stage = s_stage + (warp - 2) * 32 * kStageRowBytes;
     int t_iter = 0;
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++t_iter) {
       const int b = t_iter & 1;
       if (!mbar_wait(&tfull[b], (t_iter >> 1) & 1, abort)) break;
       tc_fence_after();
-      const int64_t row = int64_t(tile) * kBM + rloc;
-      const bool live = row < p.N;
+      if (att) {
+        const int64_t row = int64_t(tile) * kBM + rloc;
+        const uint32_t taddr = tmem + (uint32_t(q * 32) << 16) + uint32_t(b) * kAccStride;
+        // Four interleaved partial sums per vector: short dependency chains.
+        float ps[4] = {0.f, 0.f, 0.f, 0.f}, pd[4] = {0.f, 0.f, 0.f, 0.f};
+        int cur = 0;
+        for (int col0 = 0; col0 < p.N16; col0 += 32) {
+          const int width = col0 + 32 <= p.N16 ? 32 : 16;
+          uint32_t r[32];
+          if (width == 32) {
+            tmem_ld32_async(taddr + uint32_t(col0), r);
+            tmem_wait_ld();
+          } else {
+            uint32_t r16[16];
+            tmem_ld16(taddr + uint32_t(col0), r16);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) r[e] = r16[e];
+          }
+          for (int sub = 0; sub < width; sub += 16) {
+            const int c0 = col0 + sub;
+            // A 16-column chunk lies in one head (C % 16 == 0 or H == 1).
+            const int hd = p.H == 1 ? 0 : c0 / p.C;
+            if (hd != cur) {
+              if (row < p.N) {
+                p.asrc[size_t(row) * p.H + cur] = (ps[0] + ps[1]) + (ps[2] + ps[3]);
+                p.adst[size_t(row) * p.H + cur] = (pd[0] + pd[1]) + (pd[2] + pd[3]);
+              }
+#pragma unroll
+              for (int j = 0; j < 4; ++j) ps[j] = pd[j] = 0.f;
+              cur = hd;
+            }
+            const float4* ws = reinterpret_cast<const float4*>(s_att + c0);
+            const float4* wd = reinterpret_cast<const float4*>(s_att + kMaxF + c0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float4 a = ws[j], c = wd[j];
+              const float v0 = __uint_as_float(r[sub + 4 * j]), v1 = __uint_as_float(r[sub + 4 * j + 1]);
+              const float v2 = __uint_as_float(r[sub + 4 * j + 2]), v3 = __uint_as_float(r[sub + 4 * j + 3]);
+              ps[0] = fmaf(v0, a.x, ps[0]); ps[1] = fmaf(v1, a.y, ps[1]);
+              ps[2] = fmaf(v2, a.z, ps[2]); ps[3] = fmaf(v3, a.w, ps[3]);
+              pd[0] = fmaf(v0, c.x, pd[0]); pd[1] = fmaf(v1, c.y, pd[1]);
+              pd[2] = fmaf(v2, c.z, pd[2]); pd[3] = fmaf(v3, c.w, pd[3]);
+            }
+          }
+        }
+        if (row < p.N) {
+          p.asrc[size_t(row) * p.H + cur] = (ps[0] + ps[1]) + (ps[2] + ps[3]);
+          p.adst[size_t(row) * p.H + cur] = (pd[0] + pd[1]) + (pd[2] + pd[3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
+    }
+  } else {
+    // Output epilogue: convert one tile row per thread into padded shared
+    // memory, release the accumulator, then write this warp's 32 rows with
+    // one coalesced store per row.
+    const int q = warp & 3;
+    const int esize = p.h_bf16 ? 2 : 4;
+    const int pass_cols = 512 / esize;  // columns staged per pass
+    unsigned char* stage = s_stage + (warp - 2 - kAttWarps) * 32 * kStageRowBytes;
+    int t_iter = 0;
+    for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++t_iter) {
+      const int b = t_iter & 1;
+      if (!mbar_wait(&tfull[b], (t_iter >> 1) & 1, abort)) break;
+      tc_fence_after();
       const uint32_t taddr = tmem + (uint32_t(q * 32) << 16) + uint32_t(b) * kAccStride;
-      float run_s = 0.f, run_d = 0.f;
-      int cur = 0;
       for (int p0 = 0; p0 < p.N16; p0 += pass_cols) {
         const int p1 = min(p.N16, p0 + pass_cols);
-        int col0 = p0;
-        for (; col0 < p1; col0 += 64) {
-          // 64 columns per tcgen05.wait::ld when they fit, else 16 at a time.
+        for (int col0 = p0; col0 < p1;) {
           const int width = (col0 + 64 <= p1) ? 64 : 16;
           uint32_t r[64];
           if (width == 64) {
@@ -352,43 +430,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int e = 0; e < 16; ++e) r[e] = r16[e];
           }
           for (int sub = 0; sub < width; sub += 16) {
-            const int c0 = col0 + sub;
-            float v[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(r[sub + e]);
-            if (att && live) {
-              // Heads are contiguous column ranges; a 16-column chunk lies in
-              // one head (C % 16 == 0 or H == 1), so the sums run per head.
-              const int hd = p.H == 1 ? 0 : c0 / p.C;
-              if (hd != cur) {
-                p.asrc[size_t(row) * p.H + cur] = run_s;
-                p.adst[size_t(row) * p.H + cur] = run_d;
-                run_s = run_d = 0.f;
-                cur = hd;
-              }
-#pragma unroll
-              for (int e = 0; e < 16; ++e) {
-                const float ws = c0 + e < p.F ? s_att[c0 + e] : 0.f;
-                const float wd = c0 + e < p.F ? s_att[kMaxF + c0 + e] : 0.f;
-                run_s = fmaf(v[e], ws, run_s);
-                run_d = fmaf(v[e], wd, run_d);
-              }
-            }
-            unsigned char* srow = stage + lane * kStageRowBytes + (c0 - p0) * esize;
+            unsigned char* srow = stage + lane * kStageRowBytes + (col0 + sub - p0) * esize;
+            const uint32_t* rr = r + sub;
             if (p.h_bf16) {
               uint4* o4 = reinterpret_cast<uint4*>(srow);
-              o4[0] = make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]),
-                                 pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
-              o4[1] = make_uint4(pack_bf16(v[8], v[9]), pack_bf16(v[10], v[11]),
-                                 pack_bf16(v[12], v[13]), pack_bf16(v[14], v[15]));
+              o4[0] = make_uint4(pack_bf16(__uint_as_float(rr[0]), __uint_as_float(rr[1])),
+                                 pack_bf16(__uint_as_float(rr[2]), __uint_as_float(rr[3])),
+                                 pack_bf16(__uint_as_float(rr[4]), __uint_as_float(rr[5])),
+                                 pack_bf16(__uint_as_float(rr[6]), __uint_as_float(rr[7])));
+              o4[1] = make_uint4(pack_bf16(__uint_as_float(rr[8]), __uint_as_float(rr[9])),
+                                 pack_bf16(__uint_as_float(rr[10]), __uint_as_float(rr[11])),
+                                 pack_bf16(__uint_as_float(rr[12]), __uint_as_float(rr[13])),
+                                 pack_bf16(__uint_as_float(rr[14]), __uint_as_float(rr[15])));
             } else {
-              float4* o4 = reinterpret_cast<float4*>(srow);
+              uint4* o4 = reinterpret_cast<uint4*>(srow);
 #pragma unroll
               for (int e = 0; e < 4; ++e)
-                o4[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+                o4[e] = make_uint4(rr[4 * e], rr[4 * e + 1], rr[4 * e + 2], rr[4 * e + 3]);
             }
           }
-          if (width == 16) col0 -= 48;  // advance by 16 for the tail chunks
+          col0 += width;
         }
         if (p1 >= p.N16) {
           // Accumulator fully read: hand it back to the MMA warp.
@@ -397,7 +458,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) mbar_arrive(&tempty[b]);
         }
         __syncwarp();
-        // Coalesced write-out of this warp's 32 rows, columns [p0, min(F, p1)).
         const int cols = min(p.F, p1) - p0;
         if (cols > 0) {
           const int bytes = cols * esize;
@@ -420,10 +480,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         __syncwarp();
-      }
-      if (att && live) {
-        p.asrc[size_t(row) * p.H + cur] = run_s;
-        p.adst[size_t(row) * p.H + cur] = run_d;
       }
     }
   }
@@ -498,6 +554,7 @@ int proj_tc_try(gnnc_ctx_t* ctx, const void* x, int64_t ldx, const void* w, int6
 
   const int N16 = int((F + 15) / 16 * 16);
   CUtensorMap map_x, map_w;
+  if (att && H > kMaxF / 16) return kProjTcDeclined;
   if (!make_map(enc, &map_x, x, K, N, ldx, kBM) || !make_map(enc, &map_w, w, K, F, ldw, N16))
     return kProjTcDeclined;
 
@@ -519,13 +576,21 @@ int proj_tc_try(gnnc_ctx_t* ctx, const void* x, int64_t ldx, const void* w, int6
   p.adst = adst;
   p.err = ctx->dev_words + 3;
 
-  const size_t stage_bytes = size_t(kBM) * kBK * 2 + size_t(N16) * kBK * 2;
-  static_assert((kBM * kBK * 2) % 1024 == 0, "stage base alignment");
-  if (stage_bytes % 1024 != 0) return kProjTcDeclined;  // keeps every stage 1024-byte aligned
-  size_t smem = 1024 + kStages * stage_bytes + kBarrierBytes + 16 + 2 * kMaxF * sizeof(float) +
-                size_t(kEpiWarps) * 32 * kStageRowBytes;
+  const size_t a_bytes = size_t(kBM) * kBK * 2;
+  const size_t b_bytes = size_t(N16) * kBK * 2;
+  if (a_bytes % 1024 || b_bytes % 1024) return kProjTcDeclined;  // stage alignment
+  p.w_resident = size_t(p.nkb) * b_bytes <= size_t(kResidentWBytes) ? 1 : 0;
+  p.stages = p.w_resident ? kStagesResident : kStagesStream;
+  const size_t stage_bytes = p.w_resident ? a_bytes : a_bytes + b_bytes;
+  size_t smem = 1024 + (p.w_resident ? size_t(p.nkb) * b_bytes : 0) + size_t(p.stages) * stage_bytes +
+                kBarrierBytes + 16 + 2 * kMaxF * sizeof(float) +
+                size_t(kOutWarps) * 32 * kStageRowBytes;
   // At least 120 KB, so two CTAs never share an SM (each takes all 512 TMEM columns).
   if (smem < 120 * 1024) smem = 120 * 1024;
+  int max_smem = 0;
+  GNNC_CUDA_TRY(ctx, cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin,
+                                            ctx->device));
+  if (smem > size_t(max_smem)) return kProjTcDeclined;
   GNNC_CUDA_TRY(ctx, cudaFuncSetAttribute(proj_tc_kernel,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   const int grid = p.n_tiles < ctx->num_sms ? p.n_tiles : ctx->num_sms;
