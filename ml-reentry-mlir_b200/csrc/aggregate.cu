@@ -191,6 +191,30 @@ __device__ __forceinline__ void store_vec(void* out, int dtype, size_t idx, cons
   }
 }
 
+// c{0,1} += a * b{0,1} as one packed fp32x2 FMA (same rounding as two fmaf).
+__device__ __forceinline__ void ffma2(float& c0, float& c1, float a, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
+      "mov.b64 ra, {%2, %2};\n\t"
+      "mov.b64 rb, {%3, %4};\n\t"
+      "mov.b64 rc, {%0, %1};\n\t"
+      "fma.rn.f32x2 rc, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rc;\n\t}"
+      : "+f"(c0), "+f"(c1)
+      : "f"(a), "f"(b0), "f"(b1));
+}
+
+// acc[e] += a * x[e] for one vector of features.
+template <int VEC>
+__device__ __forceinline__ void fma_vec(float* acc, float a, const float* x) {
+  if constexpr (VEC % 2 == 0) {
+#pragma unroll
+    for (int e = 0; e < VEC; e += 2) ffma2(acc[e], acc[e + 1], a, x[e], x[e + 1]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) acc[e] = fmaf(a, x[e], acc[e]);
+  }
+}
+
 template <typename TH, int VEC, int LPG, int NV>
 struct Agg {
   static constexpr int G = 32 / LPG;  // edge groups per warp
@@ -294,8 +318,7 @@ struct Agg {
           for (int v = 0; v < NV; ++v) {
             const float a = s_p[(j + u * G) * p.HS + hv[v]];
             s_acc[v] += a;
-#pragma unroll
-            for (int e = 0; e < VEC; ++e) acc[v][e] = fmaf(a, hvv[u][v][e], acc[v][e]);
+            fma_vec<VEC>(acc[v], a, hvv[u][v]);
           }
       }
       for (; j < n; j += G) {
@@ -307,8 +330,7 @@ struct Agg {
           if (!vok[v]) continue;
           float x[VEC];
           VecLoad<TH, VEC>::run(r + voff[v], x);
-#pragma unroll
-          for (int e = 0; e < VEC; ++e) acc[v][e] = fmaf(a, x[e], acc[v][e]);
+          fma_vec<VEC>(acc[v], a, x);
         }
       }
       __syncwarp();
