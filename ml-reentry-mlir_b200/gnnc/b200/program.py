@@ -406,8 +406,11 @@ class B200Executable:
         self._graphs[key] = (graph, g)
         return g
 
-    def run_device(self, x: torch.Tensor, graph: torch.Tensor) -> torch.Tensor:
-        """Forward on device-resident (or host) inputs; returns the device output."""
+    def run_device(self, x: torch.Tensor, graph: torch.Tensor, events: list | None = None) -> torch.Tensor:
+        """Forward on device-resident (or host) inputs; returns the device output.
+
+        events: if a list, receives per layer a (projection_start, aggregation_start,
+        end) triple of recorded CUDA events (for per-layer timing)."""
         dt = self.program.feature_dtype
         n = x.size(0)
         h_in = to_device_features(x, dt, self.device)
@@ -415,10 +418,17 @@ class B200Executable:
         with torch.cuda.device(self.device):
             for i, (layer, (w, asrc_w, adst_w, bias)) in enumerate(zip(layers, self._weights, strict=True)):
                 g = self._graph_for(graph, n, layer)
+                ev = None
+                if events is not None:
+                    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+                    ev[0].record()
+                    events.append(ev)
                 last = i == len(layers) - 1
                 out_dtype = self.program.output_dtype if last else dt
                 if layer.kind == "gcn":
                     h = rt.proj(h_in, w, out_dtype=dt)
+                    if ev:
+                        ev[1].record()
                     h_in = rt.gcn_aggregate(
                         g.plan, g.rowptr, g.col, g.w, h, bias=bias, act=layer.act,
                         log_softmax=layer.log_softmax, out_dtype=out_dtype,
@@ -426,12 +436,20 @@ class B200Executable:
                 else:
                     h, asrc, adst = rt.proj(h_in, w, att_src=asrc_w, att_dst=adst_w,
                                             heads=layer.heads, out_dtype=dt)
+                    if ev:
+                        ev[1].record()
                     h_in = rt.gat_aggregate(
                         g.plan, g.rowptr, g.col, h, asrc, adst, heads=layer.heads,
                         negative_slope=layer.negative_slope, concat=layer.concat, bias=bias,
                         act=layer.act, log_softmax=layer.log_softmax, out_dtype=out_dtype,
                     )
+                if ev:
+                    ev[2].record()
         return h_in
+
+    def graph_edges(self, graph: torch.Tensor, num_nodes: int) -> list[int]:
+        """Stored edges (self-loops included) each layer aggregates over."""
+        return [self._graph_for(graph, num_nodes, layer).num_edges for layer in self.program.layers]
 
     def __call__(self, *inputs: torch.Tensor) -> list[torch.Tensor]:
         if len(inputs) != 2:

@@ -25,6 +25,8 @@ from gnnc.examples import MODELS_DIR, available
 
 
 def _time_forward(lowered, inputs, warmup: int, iters: int) -> dict:
+    """CUDA-event timing of the device-resident forward (graph already on the
+    device), plus per-layer projection / aggregation times and edges/s."""
     import torch
 
     x, graph = inputs
@@ -42,7 +44,22 @@ def _time_forward(lowered, inputs, warmup: int, iters: int) -> dict:
         stops[i].record()
     torch.cuda.synchronize(dev)
     ms = sorted(s.elapsed_time(e) for s, e in zip(starts, stops, strict=True))
-    return {"median_ms": ms[len(ms) // 2], "p90_ms": ms[int(len(ms) * 0.9)], "iters": iters}
+    # per-layer breakdown (separate, event-instrumented passes)
+    per = None
+    for _ in range(max(3, iters // 10)):
+        evs: list = []
+        lowered.run_device(xd, gd, events=evs)
+        torch.cuda.synchronize(dev)
+        cur = [(a.elapsed_time(b), b.elapsed_time(c)) for a, b, c in evs]
+        per = cur if per is None else [(min(p0, c0), min(p1, c1)) for (p0, p1), (c0, c1) in zip(per, cur)]
+    edges = lowered.graph_edges(gd, x.size(0))
+    layers = [
+        {"layer": i + 1, "proj_ms": pj, "agg_ms": ag, "edges": e, "agg_edges_per_s": e / (ag / 1e3),
+         "nodes_per_s": x.size(0) / ((pj + ag) / 1e3)}
+        for i, ((pj, ag), e) in enumerate(zip(per, edges))
+    ]
+    return {"median_ms": ms[len(ms) // 2], "p90_ms": ms[int(len(ms) * 0.9)], "iters": iters,
+            "layers": layers}
 
 
 def main(argv: list[str] | None = None) -> int:
@@ -59,6 +76,7 @@ def main(argv: list[str] | None = None) -> int:
     parser.add_argument("--time", action="store_true", help="time the forward with CUDA events")
     parser.add_argument("--warmup", type=int, default=20)
     parser.add_argument("--iters", type=int, default=100)
+    parser.add_argument("--json", action="store_true", help="also print the timing as one JSON line")
     args = parser.parse_args(argv)
 
     print(f"gnnc-bench {__version__}")
@@ -101,6 +119,14 @@ def main(argv: list[str] | None = None) -> int:
     actual = outs[0].cpu().numpy()
     if timing:
         print(f"  forward  : median {timing['median_ms']:.3f} ms, p90 {timing['p90_ms']:.3f} ms")
+        for lay in timing["layers"]:
+            print(f"  layer {lay['layer']}  : proj {lay['proj_ms']:.3f} ms, agg {lay['agg_ms']:.3f} ms, "
+                  f"{lay['edges']} edges, {lay['agg_edges_per_s'] / 1e9:.2f} G edges/s (agg), "
+                  f"{lay['nodes_per_s'] / 1e6:.1f} M nodes/s")
+        if args.json:
+            import json
+
+            print(json.dumps({"model": args.model, "dataset": args.dataset, **timing}))
     if ref is None:
         print(f"  out shape: {actual.shape} (not checked)")
         return 0
