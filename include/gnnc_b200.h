@@ -247,6 +247,32 @@ GNNC_API int gnnc_gat_aggregate_noalloc(gnnc_ctx_t* ctx, const gnnc_plan_t* plan
                                         const float* bias, int act, int log_softmax, void* out,
                                         int out_dtype, int64_t ldo);
 
+/* ------------------------------------------------------------------------ */
+/* Peer memory (multi-GPU exchange read straight from the owner's HBM)       */
+/* ------------------------------------------------------------------------ */
+/* The reference has no multi-GPU path (internal-docs/project-summary.md:105);
+ * these replace nothing there. With one process per GPU, a rank exports the
+ * device buffer holding the rows it owns and every other rank maps it, so the
+ * projection reads remote input rows over NVLink inside its own tile loads
+ * (TMA without multicast) instead of after an all-gather.
+ *   gnnc_peer_export : handle (GNNC_PEER_HANDLE_BYTES bytes, opaque, to be sent
+ *                      to the other ranks) and the offset of ptr inside its
+ *                      allocation; ptr must lie in a cudaMalloc allocation of
+ *                      ctx's device (GNNC_ERR_INVALID / GNNC_ERR_CUDA otherwise)
+ *   gnnc_peer_open   : maps another process's exported buffer into ctx's
+ *                      device; *ptr = the exported ptr's address here
+ *   gnnc_peer_copy   : bytes from src to dst on ctx's stream, either side a
+ *                      mapping (a copy-engine transfer; no SM is used)
+ *   gnnc_peer_close  : unmaps (ptr and offset as returned / passed to open)
+ * The exporter keeps its buffer alive until every importer has closed it, and
+ * the ranks order writes and reads of the buffer themselves (e.g. a
+ * stream-ordered collective between writing and reading). */
+#define GNNC_PEER_HANDLE_BYTES 64
+GNNC_API int gnnc_peer_export(gnnc_ctx_t* ctx, const void* ptr, void* handle, uint64_t* offset);
+GNNC_API int gnnc_peer_open(gnnc_ctx_t* ctx, const void* handle, uint64_t offset, void** ptr);
+GNNC_API int gnnc_peer_copy(gnnc_ctx_t* ctx, void* dst, const void* src, size_t bytes);
+GNNC_API int gnnc_peer_close(gnnc_ctx_t* ctx, void* ptr, uint64_t offset);
+
 #ifdef __cplusplus
 }
 #endif

@@ -2,15 +2,32 @@
 
 The reference has no multi-GPU path (multi-GPU is deferred,
 internal-docs/project-summary.md:105). Here a layer runs on `world` GPUs, one
-process per GPU:
+process per GPU, each owning a set of destination rows with its slice of the
+CSR (all source columns stay global). The layer's one exchange step is an
+all-gather over NCCL of one side of the projection, whichever is narrower:
 
-  1. rank r owns destination rows [r*R, min(N, (r+1)*R)), R = ceil(N / world),
-     with its slice of the CSR (all source columns stay global);
-  2. each rank projects its own rows into its R-row slot of a [world*R, F]
-     table (its slot of the all-gather buffer, so no copy is needed);
-  3. the table (and GAT's a_src) is all-gathered over NCCL - the path's one
-     exchange step;
-  4. each rank aggregates its rows from the gathered table.
+* output exchange (`RowRange`): rank r owns rows [r*R, min(N, (r+1)*R)),
+  R = ceil(N / world); it projects its own rows into its R-row slot of a
+  [world*R, F] table (its slot of the all-gather buffer, so no copy is
+  needed), the table (and GAT's a_src) is all-gathered, and each rank
+  aggregates its rows. Bytes exchanged per row: F (+ H for GAT) values.
+
+* peer reads (`PeerRows`): rank r owns rows [r*R, (r+1)*R) and their input
+  rows; every rank maps every other rank's input buffer (CUDA IPC) and its
+  projection reads the remote rows over NVLink inside its own tile loads,
+  writing h for all rows locally. No collective moves data; two one-word
+  all-reduces per layer order the buffer's writes and the peers' reads.
+  Bytes over NVLink per row: K input values, as for the input exchange, but
+  without a separate copy pass.
+
+* input exchange (`RowBlocks`): the input features X are all-gathered and
+  every rank projects all N rows itself. Bytes per row: K input values, so
+  this wins when K < F + H (a 100-wide input projected to 4 heads x 64 moves
+  208 instead of 528 bytes a row). The gather is split into `chunks` pieces so
+  that the projection of one piece overlaps the transfer of the next; for each
+  piece to land as a contiguous run of table rows in node order, ownership is
+  block-cyclic: the rows, padded to chunks*world*S, form `chunks` pieces of
+  world*S rows and rank r owns the r-th S-row block of every piece.
 
 Equal row counts keep the all-gather uniform; with node ids assigned
 independently of degree (as in the configuration-model and R-MAT workloads)
@@ -84,3 +101,166 @@ def all_gather_rows(table: torch.Tensor, rr: RowRange, group=None) -> None:
         dist.all_gather_into_tensor(table, my_slot(table, rr), group=group)
     else:  # gloo (CPU tests): the list form of the same collective
         dist.all_gather(list(table.split(rr.rows_per_rank)), my_slot(table, rr).clone(), group=group)
+
+
+# ---------------------------------------------------------------------------
+# input exchange: block-cyclic ownership
+# ---------------------------------------------------------------------------
+
+
+@dataclass(frozen=True)
+class RowBlocks:
+    rank: int
+    world: int
+    chunks: int
+    block_rows: int  # S: rows per (piece, rank) block
+    num_nodes: int
+
+    @property
+    def piece_rows(self) -> int:
+        return self.world * self.block_rows
+
+    @property
+    def padded_rows(self) -> int:
+        return self.chunks * self.piece_rows
+
+    def piece(self, c: int) -> slice:
+        """Table rows of piece c (node ids, padded past num_nodes)."""
+        return slice(c * self.piece_rows, (c + 1) * self.piece_rows)
+
+    def block(self, c: int) -> tuple[int, int]:
+        """Node range [begin, end) this rank owns in piece c (clipped to num_nodes)."""
+        b = c * self.piece_rows + self.rank * self.block_rows
+        return min(b, self.num_nodes), min(b + self.block_rows, self.num_nodes)
+
+    @property
+    def count(self) -> int:
+        """Owned rows; they are the first `count` rows of the local order
+        (block 0, block 1, ...), since a clipped block is followed only by
+        empty ones."""
+        return sum(e - b for b, e in (self.block(c) for c in range(self.chunks)))
+
+    def node_ids(self) -> torch.Tensor:
+        """Node id of every owned row, in local order."""
+        return torch.cat([torch.arange(*self.block(c), dtype=torch.int64) for c in range(self.chunks)])
+
+
+def row_blocks(num_nodes: int, world: int, rank: int, chunks: int = 1) -> RowBlocks:
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of {world}")
+    if chunks < 1:
+        raise ValueError("chunks must be >= 1")
+    S = max(1, (num_nodes + chunks * world - 1) // (chunks * world))
+    return RowBlocks(rank, world, chunks, S, num_nodes)
+
+
+def local_csr_blocks(rowptr: torch.Tensor, col: torch.Tensor, rb: RowBlocks, extra: tuple = ()):
+    """The owned rows of a CSR, in local order, rebased to start at edge 0.
+
+    Returns (rowptr_local int32 [count+1], col_local, *extra_local)."""
+    bounds = [rb.block(c) for c in range(rb.chunks)]
+    bounds = [(b, e) for b, e in bounds if e > b]
+    ptrs, cols, extras = [], [], [[] for _ in extra]
+    base = 0
+    for b, e in bounds:
+        e0, e1 = (int(v) for v in rowptr[[b, e]].tolist())
+        ptrs.append(rowptr[b:e] - e0 + base)
+        cols.append(col[e0:e1])
+        for lst, t in zip(extras, extra):
+            lst.append(t[e0:e1])
+        base += e1 - e0
+    end = torch.tensor([base], dtype=rowptr.dtype, device=rowptr.device)
+    rp = torch.cat(ptrs + [end]).to(torch.int32).contiguous()
+    out = [rp, torch.cat(cols).contiguous() if cols else col[:0].clone()]
+    out += [torch.cat(lst).contiguous() if lst else t[:0].clone() for lst, t in zip(extras, extra)]
+    return tuple(out)
+
+
+def input_table(rb: RowBlocks, width: int, dtype: torch.dtype, device) -> torch.Tensor:
+    """[padded_rows, width] table of the gathered input, in node order."""
+    return torch.empty((rb.padded_rows, width), dtype=dtype, device=device)
+
+
+def local_blocks(rb: RowBlocks, width: int, dtype: torch.dtype, device) -> torch.Tensor:
+    """[chunks*S, width] buffer of this rank's own rows (block c = rows [c*S, (c+1)*S))."""
+    return torch.zeros((rb.chunks * rb.block_rows, width), dtype=dtype, device=device)
+
+
+def gather_piece(table: torch.Tensor, local: torch.Tensor, rb: RowBlocks, c: int, group=None) -> None:
+    """All-gather piece c: every rank's block c of `local` lands in table[piece(c)].
+
+    With one rank it is a copy (no-op when `local` already is the table)."""
+    dst = table[rb.piece(c)]
+    src = local[c * rb.block_rows : (c + 1) * rb.block_rows]
+    if rb.world == 1:
+        if dst.data_ptr() != src.data_ptr():
+            dst.copy_(src)
+        return
+    import torch.distributed as dist
+
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(dst, src, group=group)
+    else:  # gloo (CPU tests): the list form of the same collective
+        dist.all_gather(list(dst.split(rb.block_rows)), src.clone(), group=group)
+
+
+def owned_rows(table: torch.Tensor, rb: RowBlocks) -> torch.Tensor:
+    """Copy of this rank's rows of a [padded_rows, W] node-order table, in local order."""
+    W = table.size(1)
+    v = table.view(rb.chunks, rb.world, rb.block_rows, W)[:, rb.rank]
+    return v.reshape(rb.chunks * rb.block_rows, W)[: rb.count]
+
+
+# ---------------------------------------------------------------------------
+# peer reads: every rank's input rows mapped into this process
+# ---------------------------------------------------------------------------
+
+
+class PeerRows:
+    """Every rank's [R, ld] input row block, addressable from this rank.
+
+    `local` is this rank's block (rows beyond its count are padding). Each rank
+    exports its block's CUDA IPC handle, the handles are all-gathered (host
+    objects over the process group), and the other ranks' blocks are mapped.
+    view(p) is rank p's live rows as a runtime.DeviceRows (this rank's own
+    block is read in place)."""
+
+    def __init__(self, local: torch.Tensor, rr: RowRange, num_nodes: int, group=None) -> None:
+        from gnnc.b200 import runtime as rt
+
+        if local.dim() != 2 or not local.is_contiguous() or local.size(0) != rr.rows_per_rank:
+            raise ValueError("local must be a contiguous [rows_per_rank, ld] block")
+        self._rt = rt
+        self.rr, self.local, self.num_nodes = rr, local, num_nodes
+        self._opened: list[tuple[int, int]] = []
+        meta: list = [None] * rr.world
+        if rr.world > 1:
+            import torch.distributed as dist
+
+            dist.all_gather_object(meta, rt.peer_export(local), group=group)
+        self.ptrs: list[int] = []
+        for p in range(rr.world):
+            if p == rr.rank:
+                self.ptrs.append(local.data_ptr())
+            else:
+                handle, off = meta[p]
+                ptr = rt.peer_open(local.device, handle, off)
+                self._opened.append((ptr, off))
+                self.ptrs.append(ptr)
+
+    def view(self, p: int, cols: int):
+        """Rank p's live rows [count_p, cols] (row stride = the block's ld)."""
+        loc = self.local
+        n = row_range(self.num_nodes, self.rr.world, p).count
+        return self._rt.DeviceRows(self.ptrs[p], n, cols, loc.size(1), loc.dtype, loc.device)
+
+    def close(self) -> None:
+        for ptr, off in self._opened:
+            self._rt.peer_close(self.local.device, ptr, off)
+        self._opened = []
+
+
+def read_order(rr: RowRange) -> list[int]:
+    """Owners in the order a rank reads them: itself first, then the next
+    ranks cyclically, so that at any moment the ranks read different peers."""
+    return [(rr.rank + k) % rr.world for k in range(rr.world)]

@@ -258,10 +258,24 @@ class DeviceGraph:
     w: torch.Tensor | None  # fp32 [E] (GCN weights) or None (GAT)
     plan: rt.Plan
     num_nodes: int
+    _chunks: dict = field(default_factory=dict, repr=False)
 
     @property
     def num_edges(self) -> int:
         return self.col.numel()
+
+    def row_chunks(self, k: int) -> list[tuple[int, int, rt.Plan]]:
+        """The rows split into k ranges of about equal edge counts, each with its
+        own plan over the (un-rebased) rowptr slice; built once per k."""
+        got = self._chunks.get(k)
+        if got is None:
+            n = self.rowptr.numel() - 1
+            targets = torch.linspace(0, self.num_edges, k + 1, device=self.rowptr.device)[1:-1]
+            cuts = torch.searchsorted(self.rowptr, targets.to(torch.int32)).tolist()
+            bounds = sorted({0, n, *(min(max(int(c), 0), n) for c in cuts)})
+            got = [(a, b, rt.Plan(self.rowptr[a : b + 1])) for a, b in zip(bounds, bounds[1:]) if b > a]
+            self._chunks[k] = got
+        return got
 
 
 def graph_from_csr(adj: torch.Tensor, device, *, cta_threshold=0, split_threshold=0) -> DeviceGraph:
@@ -360,6 +374,7 @@ class B200Executable:
             self._weights.append((w, asrc, adst, bias))
         self._graphs: dict[tuple, tuple[object, DeviceGraph]] = {}
         self._results = _PinnedResults()
+        self._copy_stream: torch.cuda.Stream | None = None
 
     def __str__(self) -> str:
         return f"b200.executable(device={self.device})\n{self.program}"
@@ -406,11 +421,23 @@ class B200Executable:
         self._graphs[key] = (graph, g)
         return g
 
-    def run_device(self, x: torch.Tensor, graph: torch.Tensor, events: list | None = None) -> torch.Tensor:
+    # Results for host inputs leave the device while the last aggregation still
+    # runs: its rows are aggregated in this many edge-balanced ranges, and each
+    # range's rows are copied to the host on a side stream as soon as they are
+    # done (graphs of at least this many edges per range; smaller ones use one).
+    host_chunks = 8
+    host_chunk_min_edges = 1 << 21
+
+    def run_device(self, x: torch.Tensor, graph: torch.Tensor, events: list | None = None,
+                   host_out=None) -> torch.Tensor:
         """Forward on device-resident (or host) inputs; returns the device output.
 
         events: if a list, receives per layer a (projection_start, aggregation_start,
-        end) triple of recorded CUDA events (for per-layer timing)."""
+        end) triple of recorded CUDA events (for per-layer timing).
+        host_out: if given, a callable (shape, dtype) -> page-locked host tensor;
+        the result is copied into it (overlapped with the last aggregation) and
+        the host tensor is returned once the copies are queued (synchronize the
+        current stream before reading it)."""
         dt = self.program.feature_dtype
         n = x.size(0)
         h_in = to_device_features(x, dt, self.device)
@@ -427,25 +454,56 @@ class B200Executable:
                 out_dtype = self.program.output_dtype if last else dt
                 if layer.kind == "gcn":
                     h = rt.proj(h_in, w, out_dtype=dt)
-                    if ev:
-                        ev[1].record()
-                    h_in = rt.gcn_aggregate(
-                        g.plan, g.rowptr, g.col, g.w, h, bias=bias, act=layer.act,
-                        log_softmax=layer.log_softmax, out_dtype=out_dtype,
-                    )
+                    asrc = adst = None
+                    width = h.size(1)
                 else:
                     h, asrc, adst = rt.proj(h_in, w, att_src=asrc_w, att_dst=adst_w,
                                             heads=layer.heads, out_dtype=dt)
-                    if ev:
-                        ev[1].record()
-                    h_in = rt.gat_aggregate(
-                        g.plan, g.rowptr, g.col, h, asrc, adst, heads=layer.heads,
-                        negative_slope=layer.negative_slope, concat=layer.concat, bias=bias,
-                        act=layer.act, log_softmax=layer.log_softmax, out_dtype=out_dtype,
-                    )
+                    width = h.size(1) if layer.concat else h.size(1) // layer.heads
+                if ev:
+                    ev[1].record()
+                out = rt.empty_rows(n, width, out_dtype, self.device)
+                if last and host_out is not None:
+                    host = host_out((n, width), out_dtype)
+                    self._aggregate_to_host(layer, g, h, asrc, adst, bias, out, host)
+                    h_in = host
+                else:
+                    self._aggregate(layer, g, g.plan, 0, n, h, asrc, adst, bias, out)
+                    h_in = out
                 if ev:
                     ev[2].record()
         return h_in
+
+    @staticmethod
+    def _aggregate(layer, g, plan, r0, r1, h, asrc, adst, bias, out) -> None:
+        """Aggregate destination rows [r0, r1) (plan covers exactly those rows)."""
+        rowptr = g.rowptr[r0 : r1 + 1]
+        if layer.kind == "gcn":
+            rt.gcn_aggregate(plan, rowptr, g.col, g.w, h, bias=bias, act=layer.act,
+                             log_softmax=layer.log_softmax, out_dtype=out.dtype,
+                             out=out[r0:r1], n_src=h.size(0))
+        else:
+            rt.gat_aggregate(plan, rowptr, g.col, h, asrc, adst[r0:r1], heads=layer.heads,
+                             negative_slope=layer.negative_slope, concat=layer.concat,
+                             bias=bias, act=layer.act, log_softmax=layer.log_softmax,
+                             out_dtype=out.dtype, out=out[r0:r1])
+
+    def _aggregate_to_host(self, layer, g, h, asrc, adst, bias, out, host) -> None:
+        k = self.host_chunks if g.num_edges >= self.host_chunks * self.host_chunk_min_edges else 1
+        cur = torch.cuda.current_stream(self.device)
+        if self._copy_stream is None:
+            self._copy_stream = torch.cuda.Stream(self.device)
+        side = self._copy_stream
+        chunks = g.row_chunks(k) if k > 1 else [(0, g.num_nodes, g.plan)]
+        for r0, r1, plan in chunks:
+            self._aggregate(layer, g, plan, r0, r1, h, asrc, adst, bias, out)
+            done = torch.cuda.Event()
+            done.record(cur)
+            side.wait_event(done)
+            with torch.cuda.stream(side):
+                host[r0:r1].copy_(out[r0:r1], non_blocking=True)
+        out.record_stream(side)
+        cur.wait_stream(side)
 
     def graph_edges(self, graph: torch.Tensor, num_nodes: int) -> list[int]:
         """Stored edges (self-loops included) each layer aggregates over."""
@@ -455,11 +513,11 @@ class B200Executable:
         if len(inputs) != 2:
             raise ValueError(f"expected (x, graph) inputs, got {len(inputs)}")
         x, graph = inputs
-        out = self.run_device(x, graph)
         if not x.is_cuda:
-            # Page-locked result buffer: the copy runs as one DMA at full rate.
-            host = self._results.take(tuple(out.shape), out.dtype)
-            host.copy_(out, non_blocking=True)
+            # Page-locked result buffer: the copies run as DMAs at full rate,
+            # overlapped with the last aggregation.
+            host = self.run_device(x, graph, host_out=self._results.take)
             torch.cuda.current_stream(self.device).synchronize()
             return [host]
+        out = self.run_device(x, graph)
         return [out.contiguous()]

@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import ctypes
 import threading
+from dataclasses import dataclass
 
 import torch
 
@@ -21,6 +22,7 @@ __all__ = [
     "ACT_ELU",
     "ACT_NONE",
     "ACT_RELU",
+    "DeviceRows",
     "Context",
     "GnncError",
     "Plan",
@@ -30,12 +32,39 @@ __all__ = [
     "gat_aggregate_noalloc",
     "gcn_aggregate",
     "gcn_norm",
+    "peer_close",
+    "peer_copy",
+    "peer_export",
+    "peer_open",
     "proj",
     "softmax_aggregate",
     "validate_csr",
 ]
 
 _DTYPES = {torch.float32: F32, torch.bfloat16: BF16}
+
+
+@dataclass(frozen=True)
+class DeviceRows:
+    """Rows of a 2-D row-major array at a raw device address that is valid on
+    `device` but not owned by torch (e.g. another process's buffer mapped by
+    peer_open). Usable as the x operand of proj."""
+
+    ptr: int
+    rows: int
+    cols: int
+    ld: int  # row stride in elements
+    dtype: torch.dtype
+    device: torch.device
+
+    def __getitem__(self, rows: slice) -> DeviceRows:
+        a, b, step = rows.indices(self.rows)
+        if step != 1:
+            raise ValueError("DeviceRows takes contiguous row slices only")
+        b = max(a, b)
+        esz = torch.empty((), dtype=self.dtype).element_size()
+        return DeviceRows(self.ptr + a * self.ld * esz, b - a, self.cols, self.ld, self.dtype,
+                          self.device)
 
 
 def _dt(t: torch.Tensor) -> int:
@@ -281,15 +310,25 @@ def proj(
 ):
     """h = x . weight^T (+ GAT attention coefficients).
 
-    x [N,K] (fp32 or bf16, padded rows allowed); weight [F,K] same dtype.
+    x [N,K] (fp32 or bf16, padded rows allowed; a tensor or DeviceRows);
+    weight [F,K] same dtype.
     Returns h [N,F] (row-padded) or (h, asrc [N,H], adst [N,H]) when att_* given.
     out / asrc_out / adst_out: optional destination tensors (e.g. this rank's
     slot of an all-gather buffer).
     """
-    _check_cuda(x, weight, att_src, att_dst)
+    if isinstance(x, DeviceRows):
+        if x.device != weight.device:
+            raise ValueError("x is mapped on another device than weight")
+        _check_cuda(weight, att_src, att_dst)
+        x_ptr, ldx, N, K = x.ptr, x.ld, x.rows, x.cols
+        if x.ld < x.cols or (x.ld * torch.empty((), dtype=x.dtype).element_size()) % 16:
+            raise ValueError("DeviceRows rows must be 16-byte aligned and ld >= cols")
+    else:
+        _check_cuda(x, weight, att_src, att_dst)
+        N, K = x.shape
+        x_ptr, ldx = x.data_ptr(), _ld(x)
     if x.dtype != weight.dtype:
         raise ValueError("x and weight must share a dtype")
-    N, K = x.shape
     F = weight.size(0)
     if weight.size(1) != K:
         raise ValueError(f"weight is {tuple(weight.shape)}, x has {K} columns")
@@ -306,7 +345,7 @@ def proj(
         att_dst = att_dst.reshape(-1).to(torch.float32).contiguous()
     Context.get(x.device).call(
         "gnnc_proj",
-        x.data_ptr(), _dt(x), _ld(x), weight.data_ptr(), _ld(weight), N, K, F,
+        x_ptr, _dt(x), ldx, weight.data_ptr(), _ld(weight), N, K, F,
         _p(att_src), _p(att_dst), heads, h.data_ptr(), _dt(h), _ld(h), _p(asrc), _p(adst),
     )
     return (h, asrc, adst) if att else h
@@ -475,3 +514,55 @@ def gat_aggregate_noalloc(
         int(concat), _p(bias), act, int(log_softmax), out.data_ptr(), _dt(out), _ld(out),
     )
     return out
+
+
+# ---------------------------------------------------------------------------
+# Peer memory (CUDA IPC)
+# ---------------------------------------------------------------------------
+
+PEER_HANDLE_BYTES = 64
+
+
+def peer_export(t: torch.Tensor) -> tuple[bytes, int]:
+    """(handle, offset) that lets another process map the buffer holding `t`."""
+    _check_cuda(t)
+    ctx = Context.get(t.device)
+    handle = ctypes.create_string_buffer(PEER_HANDLE_BYTES)
+    off = ctypes.c_uint64()
+    st = ctx.lib.gnnc_peer_export(ctx.handle, t.data_ptr(), handle, ctypes.byref(off))
+    raise_for(st, ctx.handle, "gnnc_peer_export")
+    return handle.raw, off.value
+
+
+def peer_open(device: torch.device | int, handle: bytes, offset: int) -> int:
+    """Maps another process's exported buffer on `device`; returns its address here."""
+    if len(handle) != PEER_HANDLE_BYTES:
+        raise ValueError(f"peer handle must be {PEER_HANDLE_BYTES} bytes")
+    ctx = Context.get(device)
+    ptr = ctypes.c_void_p()
+    st = ctx.lib.gnnc_peer_open(ctx.handle, handle, offset, ctypes.byref(ptr))
+    raise_for(st, ctx.handle, "gnnc_peer_open")
+    return ptr.value
+
+
+def peer_copy(dst: torch.Tensor | DeviceRows, src: torch.Tensor | DeviceRows, nbytes: int) -> None:
+    """Copies nbytes from src to dst on the current stream (either may be a
+    peer mapping; a copy-engine transfer)."""
+    dev = dst.device
+    ptr = {}
+    for name, t in (("dst", dst), ("src", src)):
+        if isinstance(t, DeviceRows):
+            cap = t.rows * t.ld * torch.empty((), dtype=t.dtype).element_size()
+            ptr[name] = t.ptr
+        else:
+            _check_cuda(t)
+            cap = t.untyped_storage().nbytes() - t.storage_offset() * t.element_size()
+            ptr[name] = t.data_ptr()
+        if nbytes > cap:
+            raise ValueError(f"{name} holds {cap} bytes, {nbytes} requested")
+    Context.get(dev).call("gnnc_peer_copy", ptr["dst"], ptr["src"], nbytes)
+
+
+def peer_close(device: torch.device | int, ptr: int, offset: int) -> None:
+    ctx = Context.get(device)
+    raise_for(ctx.lib.gnnc_peer_close(ctx.handle, ptr, offset), ctx.handle, "gnnc_peer_close")

@@ -1,10 +1,13 @@
 """Destination-row partitioning across ranks (world size 2, gloo, CPU).
 
-Each rank takes its row range and CSR slice (gnnc.b200.partition), projects its
-own rows into its slot of the gathered table, all-gathers h and a_src, and
-aggregates its rows; the stitched result must equal the single-process layer.
-The aggregation arithmetic here is the CPU oracle's; the logic under test is
-the partition / slot / all-gather bookkeeping the GPU bench uses unchanged.
+Output exchange: each rank takes its row range and CSR slice
+(gnnc.b200.partition), projects its own rows into its slot of the gathered
+table, all-gathers h and a_src, and aggregates its rows. Input exchange: each
+rank holds the input rows of its blocks, all-gathers X piece by piece,
+projects every row and aggregates its own. Either way the stitched result must
+equal the single-process layer. The aggregation arithmetic here is the CPU
+oracle's; the logic under test is the partition / slot / all-gather
+bookkeeping the GPU bench uses unchanged.
 """
 
 from __future__ import annotations
@@ -68,6 +71,73 @@ def _rank_main(rank, world, port, out_dir):
     dist.destroy_process_group()
 
 
+def _rank_main_blocks(rank, world, port, out_dir, chunks):
+    sys.path[:0] = [ROOT, os.path.join(ROOT, "ml-reentry-mlir_b200")]
+    import torch.distributed as dist
+
+    from gnnc.b200 import partition as P
+    from oracle import gnn_oracle as O
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world)
+    rowptr, col, x, W, a_s, a_d, H, C = _problem()
+    n = x.size(0)
+    rb = P.row_blocks(n, world, rank, chunks)
+    rowptr_l, col_l = P.local_csr_blocks(rowptr, col, rb)
+    ids = rb.node_ids()
+    x_loc = P.local_blocks(rb, x.size(1), torch.float64, "cpu")
+    x_loc[: rb.count] = x[ids]
+    table = P.input_table(rb, x.size(1), torch.float64, "cpu")
+    for c in range(rb.chunks):
+        P.gather_piece(table, x_loc, rb, c)
+    h = table @ W.t()
+    asrc = (h.view(-1, H, C) * a_s.view(1, H, C)).sum(-1)
+    adst = (h.view(-1, H, C) * a_d.view(1, H, C)).sum(-1)
+    out = O.gat_rows_fp64(rowptr_l, col_l, h[:n], asrc[:n], P.owned_rows(adst, rb), H)
+    np.save(os.path.join(out_dir, f"rank{rank}.npy"), out.numpy())
+    np.save(os.path.join(out_dir, f"ids{rank}.npy"), ids.numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_row_blocks_cover_every_row_once():
+    from gnnc.b200 import partition as P
+
+    for n in (1, 7, 8, 301, 1000):
+        for world in (1, 2, 3, 8):
+            for chunks in (1, 2, 4):
+                blocks = [P.row_blocks(n, world, r, chunks) for r in range(world)]
+                ids = torch.cat([b.node_ids() for b in blocks]).sort().values
+                assert torch.equal(ids, torch.arange(n))
+                for b in blocks:
+                    # owned rows are the prefix of the local order
+                    local = torch.arange(b.padded_rows).view(chunks, world, -1)[:, b.rank].reshape(-1)
+                    assert torch.equal(local[: b.count], b.node_ids())
+    # one chunk is the contiguous row range
+    for r in range(3):
+        b, rr = P.row_blocks(1000, 3, r), P.row_range(1000, 3, r)
+        assert b.block(0) == (rr.begin, rr.end)
+
+
+@pytest.mark.timeout(180)
+def test_two_rank_gloo_input_exchange_matches_single_process(tmp_path):
+    import torch.multiprocessing as mp
+
+    from oracle import gnn_oracle as O
+
+    world = 2
+    mp.spawn(_rank_main_blocks, args=(world, _free_port(), str(tmp_path), 3), nprocs=world,
+             join=True)
+    got = np.concatenate([np.load(tmp_path / f"rank{r}.npy") for r in range(world)])
+    ids = np.concatenate([np.load(tmp_path / f"ids{r}.npy") for r in range(world)])
+    rowptr, col, x, W, a_s, a_d, H, C = _problem()
+    h = x @ W.t()
+    asrc = (h.view(-1, H, C) * a_s.view(1, H, C)).sum(-1)
+    adst = (h.view(-1, H, C) * a_d.view(1, H, C)).sum(-1)
+    ref = O.gat_rows_fp64(rowptr, col, h, asrc, adst, H).numpy()
+    np.testing.assert_allclose(got, ref[ids], rtol=1e-12, atol=1e-12)
+
+
 def test_row_range_covers_every_row_once():
     from gnnc.b200 import partition as P
 
@@ -95,3 +165,15 @@ def test_two_rank_gloo_layer_matches_single_process(tmp_path):
     adst = (h.view(-1, H, C) * a_d.view(1, H, C)).sum(-1)
     ref = O.gat_rows_fp64(rowptr, col, h, asrc, adst, H).numpy()
     np.testing.assert_allclose(got, ref, rtol=1e-12, atol=1e-12)
+
+
+def test_peer_read_order_starts_local_and_spreads_owners():
+    from gnnc.b200 import partition as P
+
+    for world in (1, 2, 4, 8):
+        orders = [P.read_order(P.row_range(1000, world, r)) for r in range(world)]
+        for r, order in enumerate(orders):
+            assert order[0] == r and sorted(order) == list(range(world))
+        # at every position k of the read sequence the ranks read distinct owners
+        for k in range(world):
+            assert len({o[k] for o in orders}) == world
