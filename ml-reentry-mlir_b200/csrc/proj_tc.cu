@@ -12,11 +12,14 @@
 //   warp 1: allocates 512 TMEM columns (two 128 x 256 fp32 accumulators); one
 //     lane issues tcgen05.mma (M = 128, N = F16, K = 16 per instruction) and
 //     tcgen05.commit to release stages and publish finished tiles.
-//   warps 2-5: attention epilogue. Warp w reads TMEM lanes 32*(w%4) .. +31
-//     (one tile row per thread) and folds the per-head dot products with
-//     att_src / att_dst (fixed summation order: deterministic).
-//   warps 6-9: output epilogue. Same rows; convert, stage in padded shared
-//     memory, then one coalesced store per output row.
+//   warps 2-9: epilogue. Warp w reads TMEM lanes 32*(w%4) .. +31 (one tile
+//     row per thread) and the column half (w-2)/4 of the accumulator (halves
+//     split at a multiple of 128 bytes of output and, for GAT, at a head
+//     boundary). Per 128-byte pass of its columns it folds the per-head dot
+//     products with att_src / att_dst (fixed summation order: deterministic),
+//     converts, writes the values into a 128-byte-swizzled staging box and
+//     hands the box to a TMA bulk-tensor store (two boxes per warp in
+//     flight). The store clips rows >= N and columns >= F.
 // The two accumulators let the MMAs of tile i+1 run under the epilogue of
 // tile i. Every mbarrier wait is bounded by %globaltimer; a wait that gives up
 // raises an abort flag the other roles see, records GNNC_ERR_TIMEOUT in the
@@ -35,25 +38,26 @@ constexpr int kBK = 64;   // k-block: 64 bf16 = one 128-byte swizzle row
 constexpr int kStagesResident = 5;  // x-only stages when w stays resident
 constexpr int kStagesStream = 3;    // x + w stages otherwise
 constexpr int kMaxStages = 5;
-constexpr int kAttWarps = 4;
-constexpr int kOutWarps = 4;
-constexpr int kEpiWarps = kAttWarps + kOutWarps;
+constexpr int kEpiWarps = 8;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccStride = 256;  // TMEM columns per accumulator buffer
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s per wait
 constexpr int kMaxF = 256;
 constexpr int kResidentWBytes = 64 * 1024;
-// Per output warp: 32 rows of up to 512 bytes, padded by 16 bytes so the
-// per-thread row writes hit distinct banks.
-constexpr int kStageRowBytes = 512 + 16;
+// Output staging: one TMA store box = 32 rows x 128 bytes, two per epilogue
+// warp (1024-byte aligned: the 128-byte swizzle repeats every 8 rows).
+constexpr int kBoxRows = 32;
+constexpr int kBoxBytes = kBoxRows * 128;
+constexpr int kStagingBytes = kEpiWarps * 2 * kBoxBytes;
 // Bytes reserved for the 2*kMaxStages + 6 mbarriers (a multiple of 16).
 constexpr int kBarrierBytes = ((2 * kMaxStages + 6) * 8 + 15) / 16 * 16;
-static_assert(kStageRowBytes % 16 == 0 && kBarrierBytes % 16 == 0, "16-byte aligned regions");
-static_assert((2 * kMaxF * 4) % 16 == 0, "staging must start 16-byte aligned");
+static_assert(kBarrierBytes % 16 == 0 && kBoxBytes % 1024 == 0, "aligned regions");
 
 struct TcParams {
   int N, K, F, N16, nkb, n_tiles;
+  int cs;  // accumulator columns per epilogue half
+  int Fs;  // columns the bulk stores cover: F rounded down to 16 bytes of output
   int w_resident;  // all w k-blocks live in shared memory for the whole kernel
   int stages;
   int H, C;
@@ -130,6 +134,31 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Shared -> global bulk-tensor store of one box (rows / columns outside the
+// tensor map's extent are not written).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0,
+                                             int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until at most one committed store group still reads shared memory.
+__device__ __forceinline__ void bulk_wait_read_1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy (TMA) reads of them.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
 // 1024 bytes apart (SBO), tcgen05 descriptor version 1.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -179,6 +208,16 @@ __device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -206,9 +245,97 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
 }
 
+// Flushes the attention sums of head `hd` for this thread's row.
+__device__ __forceinline__ void att_flush(const TcParams& p, int64_t row, int hd, const float (&ps)[4],
+                                          const float (&pd)[4]) {
+  if (row < p.N) {
+    p.asrc[size_t(row) * p.H + hd] = (ps[0] + ps[1]) + (ps[2] + ps[3]);
+    p.adst[size_t(row) * p.H + hd] = (pd[0] + pd[1]) + (pd[2] + pd[3]);
+  }
+}
+
+// One 128-byte pass of an epilogue warp over W accumulator columns from c0 of
+// this thread's row (TMEM lane): attention partial sums of the heads the
+// columns belong to, conversion into the swizzled staging box (16-byte chunk
+// j of row r at chunk slot j ^ (r % 8)), and the TMA store of the box.
+template <int W, bool kBf16>
+__device__ __forceinline__ void epi_pass(const TcParams& p, const CUtensorMap* map_h,
+                                         uint32_t taddr, int c0, int64_t row, int row0,
+                                         unsigned char* box, const float* s_att, bool att,
+                                         float (&ps)[4], float (&pd)[4], int& cur, int lane) {
+  static_assert(W % 16 == 0 && W <= (kBf16 ? 64 : 32), "one 128-byte pass");
+  uint32_t r[W];
+#pragma unroll
+  for (int off = 0; off + 32 <= W; off += 32) tmem_ld32_async(taddr + uint32_t(c0 + off), r + off);
+  if constexpr (W % 32 != 0) tmem_ld16_async(taddr + uint32_t(c0 + W - 16), r + W - 16);
+  tmem_wait_ld();
+  if (att) {
+#pragma unroll
+    for (int sub = 0; sub < W; sub += 16) {
+      const int c = c0 + sub;
+      // A 16-column chunk lies in one head (C % 16 == 0 or H == 1).
+      const int hd = p.H == 1 ? 0 : c / p.C;
+      if (hd != cur) {
+        if (cur >= 0) att_flush(p, row, cur, ps, pd);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) ps[j] = pd[j] = 0.f;
+        cur = hd;
+      }
+      const float4* ws = reinterpret_cast<const float4*>(s_att + c);
+      const float4* wd = reinterpret_cast<const float4*>(s_att + kMaxF + c);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 a = ws[j], d = wd[j];
+        const float v0 = __uint_as_float(r[sub + 4 * j]), v1 = __uint_as_float(r[sub + 4 * j + 1]);
+        const float v2 = __uint_as_float(r[sub + 4 * j + 2]), v3 = __uint_as_float(r[sub + 4 * j + 3]);
+        ps[0] = fmaf(v0, a.x, ps[0]); ps[1] = fmaf(v1, a.y, ps[1]);
+        ps[2] = fmaf(v2, a.z, ps[2]); ps[3] = fmaf(v3, a.w, ps[3]);
+        pd[0] = fmaf(v0, d.x, pd[0]); pd[1] = fmaf(v1, d.y, pd[1]);
+        pd[2] = fmaf(v2, d.z, pd[2]); pd[3] = fmaf(v3, d.w, pd[3]);
+      }
+    }
+  }
+  unsigned char* srow = box + lane * 128;
+  constexpr int kChunks = kBf16 ? W / 8 : W / 4;
+#pragma unroll
+  for (int j = 0; j < kChunks; ++j) {
+    uint4 v;
+    if constexpr (kBf16) {
+      const uint32_t* q = r + 8 * j;
+      v = make_uint4(pack_bf16(__uint_as_float(q[0]), __uint_as_float(q[1])),
+                     pack_bf16(__uint_as_float(q[2]), __uint_as_float(q[3])),
+                     pack_bf16(__uint_as_float(q[4]), __uint_as_float(q[5])),
+                     pack_bf16(__uint_as_float(q[6]), __uint_as_float(q[7])));
+    } else {
+      v = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+    }
+    *reinterpret_cast<uint4*>(srow + ((j ^ (lane & 7)) << 4)) = v;
+  }
+  // Columns [Fs, F) end in a partial 16-byte chunk, which a bulk store would
+  // write whole: this thread stores them from its staged chunk instead.
+  if (p.Fs < p.F && p.Fs >= c0 && p.Fs < c0 + W && row < p.N) {
+    constexpr int kEsize = kBf16 ? 2 : 4;
+    const int jt = (p.Fs - c0) * kEsize / 16;
+    const unsigned char* chunk = srow + ((jt ^ (lane & 7)) << 4);
+    unsigned char* g = reinterpret_cast<unsigned char*>(p.h) + (size_t(row) * size_t(p.ldh) + size_t(p.Fs)) * kEsize;
+    for (int e = 0; e < p.F - p.Fs; ++e) {
+      if constexpr (kBf16)
+        reinterpret_cast<uint16_t*>(g)[e] = reinterpret_cast<const uint16_t*>(chunk)[e];
+      else
+        reinterpret_cast<uint32_t*>(g)[e] = reinterpret_cast<const uint32_t*>(chunk)[e];
+    }
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0 && row0 < p.N && c0 < p.Fs) {  // a box wholly below the last row has nothing to store
+    tma_store_2d(map_h, box, c0, row0);
+    bulk_commit();
+  }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     proj_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
-                   const TcParams p) {
+                   const __grid_constant__ CUtensorMap map_h, const TcParams p) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -216,14 +343,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int b_bytes = p.N16 * kBK * 2;              // one w k-block
   const int stage_bytes = p.w_resident ? a_bytes : a_bytes + b_bytes;  // multiple of 1024
   const int S = p.stages;
-  // Carve-up (offsets from the 1024-byte aligned base; every region starts on
-  // a multiple of 16 bytes):
-  //   [resident w: nkb * b_bytes][S stages][kBarrierBytes: mbarriers]
-  //   [16: TMEM address, abort flag][2*kMaxF floats: att_src, att_dst]
-  //   [kOutWarps * 32 rows: output staging]
+  // Carve-up (offsets from the 1024-byte aligned base; the first three regions
+  // are multiples of 1024 bytes long, the rest start on 16-byte multiples):
+  //   [resident w: nkb * b_bytes][S stages][output staging: kStagingBytes]
+  //   [kBarrierBytes: mbarriers][16: TMEM address, abort flag]
+  //   [2*kMaxF floats: att_src, att_dst]
   unsigned char* w_res = smem;
   unsigned char* stages = smem + (p.w_resident ? p.nkb * b_bytes : 0);
-  unsigned char* bar_base = stages + S * stage_bytes;
+  unsigned char* s_stage = stages + S * stage_bytes;
+  unsigned char* bar_base = s_stage + kStagingBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(bar_base);
   uint64_t* empty = full + kMaxStages;
   uint64_t* tfull = empty + kMaxStages;
@@ -233,7 +361,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_base + kBarrierBytes);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* s_att = reinterpret_cast<float*>(bar_base + kBarrierBytes + 16);  // [2][kMaxF]
-  unsigned char* s_stage = reinterpret_cast<unsigned char*>(s_att + 2 * kMaxF);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -337,151 +464,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(drain);
       mbar_wait(drain, 0, abort, false);
     }
-  } else if (warp < 2 + kAttWarps) {
-    // Attention epilogue: per-head dot products of each row with att_src / att_dst.
-    const int q = warp & 3;
-    const int rloc = q * 32 + lane;
-    int t_iter = 0;
-    for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++t_iter) {
-      const int b = t_iter & 1;
-      if (!mbar_wait(&tfull[b], (t_iter >> 1) & 1, abort)) break;
-      tc_fence_after();
-      if (att) {
-        const int64_t row = int64_t(tile) * kBM + rloc;
-        const uint32_t taddr = tmem + (uint32_t(q * 32) << 16) + uint32_t(b) * kAccStride;
-        // Four interleaved partial sums per vector: short dependency chains.
-        float ps[4] = {0.f, 0.f, 0.f, 0.f}, pd[4] = {0.f, 0.f, 0.f, 0.f};
-        int cur = 0;
-        for (int col0 = 0; col0 < p.N16; col0 += 32) {
-          const int width = col0 + 32 <= p.N16 ? 32 : 16;
-          uint32_t r[32];
-          if (width == 32) {
-            tmem_ld32_async(taddr + uint32_t(col0), r);
-            tmem_wait_ld();
-          } else {
-            uint32_t r16[16];
-            tmem_ld16(taddr + uint32_t(col0), r16);
-#pragma unroll
-            for (int e = 0; e < 16; ++e) r[e] = r16[e];
-          }
-          for (int sub = 0; sub < width; sub += 16) {
-            const int c0 = col0 + sub;
-            // A 16-column chunk lies in one head (C % 16 == 0 or H == 1).
-            const int hd = p.H == 1 ? 0 : c0 / p.C;
-            if (hd != cur) {
-              if (row < p.N) {
-                p.asrc[size_t(row) * p.H + cur] = (ps[0] + ps[1]) + (ps[2] + ps[3]);
-                p.adst[size_t(row) * p.H + cur] = (pd[0] + pd[1]) + (pd[2] + pd[3]);
-              }
-#pragma unroll
-              for (int j = 0; j < 4; ++j) ps[j] = pd[j] = 0.f;
-              cur = hd;
-            }
-            const float4* ws = reinterpret_cast<const float4*>(s_att + c0);
-            const float4* wd = reinterpret_cast<const float4*>(s_att + kMaxF + c0);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float4 a = ws[j], c = wd[j];
-              const float v0 = __uint_as_float(r[sub + 4 * j]), v1 = __uint_as_float(r[sub + 4 * j + 1]);
-              const float v2 = __uint_as_float(r[sub + 4 * j + 2]), v3 = __uint_as_float(r[sub + 4 * j + 3]);
-              ps[0] = fmaf(v0, a.x, ps[0]); ps[1] = fmaf(v1, a.y, ps[1]);
-              ps[2] = fmaf(v2, a.z, ps[2]); ps[3] = fmaf(v3, a.w, ps[3]);
-              pd[0] = fmaf(v0, c.x, pd[0]); pd[1] = fmaf(v1, c.y, pd[1]);
-              pd[2] = fmaf(v2, c.z, pd[2]); pd[3] = fmaf(v3, c.w, pd[3]);
-            }
-          }
-        }
-        if (row < p.N) {
-          p.asrc[size_t(row) * p.H + cur] = (ps[0] + ps[1]) + (ps[2] + ps[3]);
-          p.adst[size_t(row) * p.H + cur] = (pd[0] + pd[1]) + (pd[2] + pd[3]);
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[b]);
-    }
   } else {
-    // Output epilogue: convert one tile row per thread into padded shared
-    // memory, release the accumulator, then write this warp's 32 rows with
-    // one coalesced store per row.
+    // Epilogue: TMEM lanes 32*(warp%4) .. +31, column half (warp-2)/4.
     const int q = warp & 3;
-    const int esize = p.h_bf16 ? 2 : 4;
-    const int pass_cols = 512 / esize;  // columns staged per pass
-    unsigned char* stage = s_stage + (warp - 2 - kAttWarps) * 32 * kStageRowBytes;
-    int t_iter = 0;
+    const int half = (warp - 2) >> 2;
+    const int c_begin = half * p.cs;
+    const int c_end = min(p.N16, c_begin + p.cs);
+    const int pass_cols = p.h_bf16 ? 64 : 32;  // 128 bytes of output per row
+    unsigned char* boxes = s_stage + (warp - 2) * 2 * kBoxBytes;
+    int t_iter = 0, pass_no = 0;
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++t_iter) {
       const int b = t_iter & 1;
       if (!mbar_wait(&tfull[b], (t_iter >> 1) & 1, abort)) break;
       tc_fence_after();
       const uint32_t taddr = tmem + (uint32_t(q * 32) << 16) + uint32_t(b) * kAccStride;
-      for (int p0 = 0; p0 < p.N16; p0 += pass_cols) {
-        const int p1 = min(p.N16, p0 + pass_cols);
-        for (int col0 = p0; col0 < p1;) {
-          const int width = (col0 + 64 <= p1) ? 64 : 16;
-          uint32_t r[64];
-          if (width == 64) {
-            tmem_ld32_async(taddr + uint32_t(col0), r);
-            tmem_ld32_async(taddr + uint32_t(col0 + 32), r + 32);
-            tmem_wait_ld();
-          } else {
-            uint32_t r16[16];
-            tmem_ld16(taddr + uint32_t(col0), r16);
-#pragma unroll
-            for (int e = 0; e < 16; ++e) r[e] = r16[e];
-          }
-          for (int sub = 0; sub < width; sub += 16) {
-            unsigned char* srow = stage + lane * kStageRowBytes + (col0 + sub - p0) * esize;
-            const uint32_t* rr = r + sub;
-            if (p.h_bf16) {
-              uint4* o4 = reinterpret_cast<uint4*>(srow);
-              o4[0] = make_uint4(pack_bf16(__uint_as_float(rr[0]), __uint_as_float(rr[1])),
-                                 pack_bf16(__uint_as_float(rr[2]), __uint_as_float(rr[3])),
-                                 pack_bf16(__uint_as_float(rr[4]), __uint_as_float(rr[5])),
-                                 pack_bf16(__uint_as_float(rr[6]), __uint_as_float(rr[7])));
-              o4[1] = make_uint4(pack_bf16(__uint_as_float(rr[8]), __uint_as_float(rr[9])),
-                                 pack_bf16(__uint_as_float(rr[10]), __uint_as_float(rr[11])),
-                                 pack_bf16(__uint_as_float(rr[12]), __uint_as_float(rr[13])),
-                                 pack_bf16(__uint_as_float(rr[14]), __uint_as_float(rr[15])));
-            } else {
-              uint4* o4 = reinterpret_cast<uint4*>(srow);
-#pragma unroll
-              for (int e = 0; e < 4; ++e)
-                o4[e] = make_uint4(rr[4 * e], rr[4 * e + 1], rr[4 * e + 2], rr[4 * e + 3]);
-            }
-          }
-          col0 += width;
-        }
-        if (p1 >= p.N16) {
-          // Accumulator fully read: hand it back to the MMA warp.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[b]);
-        }
+      const int row0 = tile * kBM + q * 32;
+      const int64_t row = int64_t(row0) + lane;
+      float ps[4] = {0.f, 0.f, 0.f, 0.f}, pd[4] = {0.f, 0.f, 0.f, 0.f};
+      int cur = -1;
+      for (int c0 = c_begin; c0 < c_end; c0 += pass_cols, ++pass_no) {
+        const int width = min(pass_cols, c_end - c0);
+        unsigned char* box = boxes + (pass_no & 1) * kBoxBytes;
+        // the store that last read this box (two passes ago) is done reading
+        if (lane == 0) bulk_wait_read_1();
         __syncwarp();
-        const int cols = min(p.F, p1) - p0;
-        if (cols > 0) {
-          const int bytes = cols * esize;
-          const int n16 = bytes / 16;
-#pragma unroll 4
-          for (int rr = 0; rr < 32; ++rr) {
-            const int64_t grow = int64_t(tile) * kBM + q * 32 + rr;
-            if (grow >= p.N) continue;
-            unsigned char* g = reinterpret_cast<unsigned char*>(p.h) +
-                               (size_t(grow) * size_t(p.ldh) + size_t(p0)) * esize;
-            const unsigned char* sr = stage + rr * kStageRowBytes;
-            for (int j = lane; j < n16; j += 32)
-              *reinterpret_cast<uint4*>(g + j * 16) = *reinterpret_cast<const uint4*>(sr + j * 16);
-            for (int j = n16 * 16 + lane * esize; j < bytes; j += 32 * esize) {
-              if (esize == 2)
-                *reinterpret_cast<uint16_t*>(g + j) = *reinterpret_cast<const uint16_t*>(sr + j);
-              else
-                *reinterpret_cast<uint32_t*>(g + j) = *reinterpret_cast<const uint32_t*>(sr + j);
-            }
+        if (p.h_bf16) {
+          switch (width) {
+            case 64: epi_pass<64, true>(p, &map_h, taddr, c0, row, row0, box, s_att, att, ps, pd, cur, lane); break;
+            case 48: epi_pass<48, true>(p, &map_h, taddr, c0, row, row0, box, s_att, att, ps, pd, cur, lane); break;
+            case 32: epi_pass<32, true>(p, &map_h, taddr, c0, row, row0, box, s_att, att, ps, pd, cur, lane); break;
+            default: epi_pass<16, true>(p, &map_h, taddr, c0, row, row0, box, s_att, att, ps, pd, cur, lane); break;
           }
+        } else {
+          if (width == 32)
+            epi_pass<32, false>(p, &map_h, taddr, c0, row, row0, box, s_att, att, ps, pd, cur, lane);
+          else
+            epi_pass<16, false>(p, &map_h, taddr, c0, row, row0, box, s_att, att, ps, pd, cur, lane);
         }
-        __syncwarp();
       }
+      if (att && cur >= 0) att_flush(p, row, cur, ps, pd);
+      // Accumulator fully read: hand it back to the MMA warp.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
     }
+    // Every store has finished with shared memory (and global memory) before
+    // the CTA can go away.
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -519,16 +549,18 @@ EncodeTiledFn encode_fn(gnnc_ctx_t* ctx) {
   return g_encode;
 }
 
-// 2-D bf16 tensor map: inner dim `inner` (elements), `rows` rows of `ld`
-// elements, box kBK x box_rows, 128-byte swizzle, zero fill out of bounds.
+// 2-D tensor map: inner dim `inner` (elements), `rows` rows of `ld`
+// elements, box box_inner x box_rows, 128-byte swizzle, zero fill out of
+// bounds on loads, clipping on stores.
 bool make_map(EncodeTiledFn enc, CUtensorMap* map, const void* base, int64_t inner,
-              int64_t rows, int64_t ld, int box_rows) {
+              int64_t rows, int64_t ld, int box_rows, int box_inner = kBK,
+              CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, int esize = 2) {
   const cuuint64_t dims[2] = {cuuint64_t(inner), cuuint64_t(rows)};
-  const cuuint64_t strides[1] = {cuuint64_t(ld) * 2};
-  const cuuint32_t box[2] = {cuuint32_t(kBK), cuuint32_t(box_rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(ld) * cuuint64_t(esize)};
+  const cuuint32_t box[2] = {cuuint32_t(box_inner), cuuint32_t(box_rows)};
   const cuuint32_t estr[2] = {1, 1};
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
-             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  return enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -553,10 +585,34 @@ int proj_tc_try(gnnc_ctx_t* ctx, const void* x, int64_t ldx, const void* w, int6
   if (!enc) return kProjTcDeclined;
 
   const int N16 = int((F + 15) / 16 * 16);
-  CUtensorMap map_x, map_w;
+  const bool h_bf16 = h_dtype == GNNC_BF16;
+  const int h_esize = h_bf16 ? 2 : 4;
+  const int pass_cols = 128 / h_esize;
+  // Bulk stores cover whole 16-byte chunks of a row: columns [0, Fs); the
+  // epilogue writes the few columns of a partial last chunk itself.
+  const int Fs = int(F * h_esize / 16 * 16 / h_esize);
+  if (Fs == 0) return kProjTcDeclined;
+  CUtensorMap map_x, map_w, map_h;
   if (att && H > kMaxF / 16) return kProjTcDeclined;
-  if (!make_map(enc, &map_x, x, K, N, ldx, kBM) || !make_map(enc, &map_w, w, K, F, ldw, N16))
+  if (!make_map(enc, &map_x, x, K, N, ldx, kBM) || !make_map(enc, &map_w, w, K, F, ldw, N16) ||
+      !make_map(enc, &map_h, h, Fs, N, ldh, kBoxRows, pass_cols,
+                h_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                h_esize))
     return kProjTcDeclined;
+  // Column split between the two epilogue halves: about half the columns,
+  // rounded up to whole 128-byte passes and, with attention, to whole heads
+  // (a head's dot products stay in one warp).
+  int unit = pass_cols;
+  if (att && H > 1) {
+    const int c = int(C);
+    int l = unit;
+    while (l % c) l += unit;  // lcm(pass_cols, C)
+    unit = l;
+  } else if (att) {
+    unit = N16;
+  }
+  int cs = ((N16 + 1) / 2 + unit - 1) / unit * unit;
+  if (cs < unit) cs = unit;
 
   TcParams p{};
   p.N = int(N);
@@ -569,8 +625,10 @@ int proj_tc_try(gnnc_ctx_t* ctx, const void* x, int64_t ldx, const void* w, int6
   p.C = int(C);
   p.att_src = att_src;
   p.att_dst = att_dst;
+  p.cs = cs;
+  p.Fs = Fs;
   p.h = h;
-  p.h_bf16 = h_dtype == GNNC_BF16;
+  p.h_bf16 = h_bf16;
   p.ldh = ldh;
   p.asrc = asrc;
   p.adst = adst;
@@ -583,8 +641,7 @@ int proj_tc_try(gnnc_ctx_t* ctx, const void* x, int64_t ldx, const void* w, int6
   p.stages = p.w_resident ? kStagesResident : kStagesStream;
   const size_t stage_bytes = p.w_resident ? a_bytes : a_bytes + b_bytes;
   size_t smem = 1024 + (p.w_resident ? size_t(p.nkb) * b_bytes : 0) + size_t(p.stages) * stage_bytes +
-                kBarrierBytes + 16 + 2 * kMaxF * sizeof(float) +
-                size_t(kOutWarps) * 32 * kStageRowBytes;
+                kStagingBytes + kBarrierBytes + 16 + 2 * kMaxF * sizeof(float);
   // At least 120 KB, so two CTAs never share an SM (each takes all 512 TMEM columns).
   if (smem < 120 * 1024) smem = 120 * 1024;
   int max_smem = 0;
@@ -594,7 +651,7 @@ int proj_tc_try(gnnc_ctx_t* ctx, const void* x, int64_t ldx, const void* w, int6
   GNNC_CUDA_TRY(ctx, cudaFuncSetAttribute(proj_tc_kernel,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   const int grid = p.n_tiles < ctx->num_sms ? p.n_tiles : ctx->num_sms;
-  proj_tc_kernel<<<grid, kThreads, smem, ctx->stream>>>(map_x, map_w, p);
+  proj_tc_kernel<<<grid, kThreads, smem, ctx->stream>>>(map_x, map_w, map_h, p);
   GNNC_CUDA_TRY(ctx, cudaGetLastError());
   return GNNC_OK;
 }
