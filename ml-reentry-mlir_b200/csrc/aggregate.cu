@@ -401,9 +401,144 @@ struct Agg {
   }
 };
 
-template <typename TH, int VEC, int LPG, int NV>
+// Edge loop specialised for the widest common layout: bf16 h with 8 features
+// (one 16-byte load) per lane and the whole warp on one edge at a time
+// (F = 256), and a compile-time head count KH (0: GCN edge weights). Same
+// arithmetic, in the same order, as Agg<bf16, 8, 32, 1>::range; what changes
+// is the instruction count per edge: the head loops unroll, the edges of a
+// chunk are visited in groups of eight at constant shared-memory offsets with
+// eight row loads in flight, and a row address is one wide multiply-add from
+// a per-lane base.
+template <int KH>
+struct AggFast {
+  static constexpr int HS = KH == 0 ? 1 : (KH | 1);
+
+  static __device__ __forceinline__ void fma_row(float (&acc)[8], float a, const uint4& v) {
+    ffma2(acc[0], acc[1], a, bf16_lo(v.x), bf16_hi(v.x));
+    ffma2(acc[2], acc[3], a, bf16_lo(v.y), bf16_hi(v.y));
+    ffma2(acc[4], acc[5], a, bf16_lo(v.z), bf16_hi(v.z));
+    ffma2(acc[6], acc[7], a, bf16_lo(v.w), bf16_hi(v.w));
+  }
+
+  static __device__ __forceinline__ void range(const AggParams& p, int64_t row, int eb, int ee,
+                                               float (&acc)[1][8], float (&s_acc)[1],
+                                               float& m_reg, int32_t* s_col, float* s_p,
+                                               const int (&hv)[1], int lane) {
+    const char* hlane = reinterpret_cast<const char*>(p.h) + lane * 16;
+    const uint32_t ldh_b = uint32_t(p.ldh) * 2u;
+    const float* s_ph = s_p + hv[0];
+    float sc_reg = 1.f;
+    float ad_reg = 0.f;
+    if (KH > 0 && p.mode == MODE_GAT && lane < KH) ad_reg = __ldg(p.adst + size_t(row) * KH + lane);
+    for (int cb = eb; cb < ee; cb += 32) {
+      const int k = cb + lane;
+      bool valid = k < ee;
+      int src = valid ? __ldg(p.col + k) : 0;
+      if (valid && unsigned(src) >= unsigned(p.n_src)) {
+        atomicOr(p.counters + 2, 1);
+        valid = false;
+        src = 0;
+      }
+      s_col[lane] = src;
+      if constexpr (KH == 0) {
+        s_p[lane] = valid ? __ldg(p.w + k) : 0.f;
+      } else {
+        // Lanes past the chunk's last edge read a valid row too: a_src of
+        // node 0, or the chunk's first score row.
+        const float* xs = p.mode == MODE_GAT ? p.asrc + size_t(src) * KH
+                                             : p.scores + size_t(valid ? k : cb) * KH;
+        float x[KH];
+        if constexpr (KH == 4) {
+          const float4 v = __ldg(reinterpret_cast<const float4*>(xs));
+          x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+        } else if constexpr (KH == 2) {
+          const float2 v = __ldg(reinterpret_cast<const float2*>(xs));
+          x[0] = v.x; x[1] = v.y;
+        } else {
+#pragma unroll
+          for (int hd = 0; hd < KH; ++hd) x[hd] = __ldg(xs + hd);
+        }
+        bool rescale = false;
+#pragma unroll
+        for (int hd = 0; hd < KH; ++hd) {
+          // Every lane takes part in the shuffles and the reduction: `valid`
+          // differs across lanes, so they stay outside its branch.
+          const float ad = __shfl_sync(kFull, ad_reg, hd);
+          float e = -INFINITY;
+          if (valid) {
+            if (p.mode == MODE_GAT) {
+              const float t = x[hd] + ad;
+              e = t > 0.f ? t : t * p.slope;
+            } else {
+              e = x[hd];
+            }
+          }
+          const float cmax = warp_max_redux(e);
+          const float m_old = __shfl_sync(kFull, m_reg, hd);
+          const float m_new = fmaxf(m_old, cmax);
+          const float pr = valid ? __expf(e - m_new) : 0.f;
+          const float sc = __expf(m_old - m_new);
+          if (lane == hd) {
+            sc_reg = sc;
+            m_reg = m_new;
+          }
+          rescale |= (cb != eb) && (m_new != m_old);
+          s_p[lane * HS + hd] = pr;
+        }
+        if (rescale) {  // warp-uniform: m_new and m_old are the same in every lane
+          const float sc = __shfl_sync(kFull, sc_reg, hv[0]);
+          s_acc[0] *= sc;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[0][e] *= sc;
+        }
+      }
+      __syncwarp();
+      const int n = min(32, ee - cb);
+      int j = 0;
+      for (; j + 8 <= n; j += 8) {
+        const int32_t* cj = s_col + j;
+        const float* pj = s_ph + j * HS;
+        uint4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          v[u] = __ldg(reinterpret_cast<const uint4*>(hlane + size_t(uint32_t(cj[u])) * ldh_b));
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float a = pj[u * HS];
+          s_acc[0] += a;
+          fma_row(acc[0], a, v[u]);
+        }
+      }
+      for (; j < n; ++j) {
+        const uint4 v =
+            __ldg(reinterpret_cast<const uint4*>(hlane + size_t(uint32_t(s_col[j])) * ldh_b));
+        const float a = s_ph[j * HS];
+        s_acc[0] += a;
+        fma_row(acc[0], a, v);
+      }
+      __syncwarp();
+    }
+  }
+};
+
+// Selects the edge loop: the specialised one for KH >= 0, the generic otherwise.
+template <typename TH, int VEC, int LPG, int NV, int KH>
+struct EdgeLoop {
+  using type = Agg<TH, VEC, LPG, NV>;
+};
+template <int KH>
+struct EdgeLoop<__nv_bfloat16, 8, 32, 1, KH> {
+  using type = AggFast<KH>;
+};
+template <>
+struct EdgeLoop<__nv_bfloat16, 8, 32, 1, -1> {
+  using type = Agg<__nv_bfloat16, 8, 32, 1>;
+};
+
+template <typename TH, int VEC, int LPG, int NV, int KH = -1>
 __global__ void __launch_bounds__(kThreads, 4) agg_kernel(const AggParams p) {
   using A = Agg<TH, VEC, LPG, NV>;
+  using L = typename EdgeLoop<TH, VEC, LPG, NV, KH>::type;
   extern __shared__ float smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -457,7 +592,7 @@ __global__ void __launch_bounds__(kThreads, 4) agg_kernel(const AggParams p) {
       for (int e = 0; e < VEC; ++e) acc[v][e] = 0.f;
     }
     float m_reg = -INFINITY;
-    A::range(p, row, wb, we, acc, s_acc, m_reg, s_col, s_p, hv, lane);
+    L::range(p, row, wb, we, acc, s_acc, m_reg, s_col, s_p, hv, lane);
     A::group_reduce(acc, s_acc);
     A::spill(p, acc, one, s_row, lane);
     if (lane < kHMax) s_wm[warp * kHMax + lane] = m_reg;
@@ -521,7 +656,7 @@ __global__ void __launch_bounds__(kThreads, 4) agg_kernel(const AggParams p) {
       }
       float m_reg = -INFINITY;
       if (ee > eb) {
-        A::range(p, r, eb, ee, acc, s_acc, m_reg, s_col, s_p, hv, lane);
+        L::range(p, r, eb, ee, acc, s_acc, m_reg, s_col, s_p, hv, lane);
         A::group_reduce(acc, s_acc);
       }
       const bool divide = softmax && ee > eb;
@@ -668,7 +803,24 @@ int run_aggregate(gnnc_ctx_t* ctx, const Launch& L, AggParams p) {
                            "feature width %d too large for the row kernel (vector width %d)", p.F,
                            vec);
   KernelFn fn = nullptr;
-  if (L.h_dtype == GNNC_BF16)
+  if (L.h_dtype == GNNC_BF16 && vec == 8 && p.F == 256) {
+    // Specialised edge loop for a compile-time head count. It reads a_src
+    // rows (or score rows) as one vector: they must be aligned to it.
+    const int kh = p.mode == MODE_GCN ? 0 : p.H;
+    const uintptr_t xs = reinterpret_cast<uintptr_t>(p.mode == MODE_GAT ? p.asrc : p.scores);
+    const bool xs_ok = kh == 4 ? xs % 16 == 0 : (kh == 2 ? xs % 8 == 0 : true);
+    switch (xs_ok ? kh : -1) {
+      case 0: fn = agg_kernel<__nv_bfloat16, 8, 32, 1, 0>; break;
+      case 1: fn = agg_kernel<__nv_bfloat16, 8, 32, 1, 1>; break;
+      case 2: fn = agg_kernel<__nv_bfloat16, 8, 32, 1, 2>; break;
+      case 4: fn = agg_kernel<__nv_bfloat16, 8, 32, 1, 4>; break;
+      case 8: fn = agg_kernel<__nv_bfloat16, 8, 32, 1, 8>; break;
+      default: break;
+    }
+  }
+  if (fn) {
+    // specialised loop chosen
+  } else if (L.h_dtype == GNNC_BF16)
     fn = vec == 8 ? pick_layout<__nv_bfloat16, 8>(lpg, nv) : pick_layout<__nv_bfloat16, 1>(lpg, nv);
   else
     fn = vec == 4 ? pick_layout<float, 4>(lpg, nv) : pick_layout<float, 1>(lpg, nv);

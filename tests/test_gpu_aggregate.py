@@ -203,3 +203,52 @@ def test_bad_column_is_skipped_and_reported(device):
     with pytest.raises(GnncInvalidArgument):
         rt.Context.get(device).synchronize()
     rt.Context.get(device).synchronize()  # flag cleared
+
+
+@pytest.mark.parametrize("H,C,concat", [(1, 256, True), (2, 128, True), (8, 32, True),
+                                         (4, 64, False), (3, 256, True)])
+def test_gat_bf16_256_wide_head_counts(device, H, C, concat):
+    """bf16 rows of 256 features (one 16-byte load per lane) for every head
+    count the compile-time edge loops cover, a mean-over-heads epilogue, and
+    a width that takes the generic loop (3 x 256 features)."""
+    out, ref, _ = _gat_case(device, 1800, 30000, H, C, torch.bfloat16, ((4, 7000), (6, 900)), 0,
+                            0, concat, act=2, lsm=False, seed=40 + H)
+    assert_close(out, ref)
+
+
+def test_softmax_aggregate_bf16_256_wide(device):
+    """Given scores [E, 4] with bf16 256-wide rows (the score-row vector loads,
+    including the lanes past a chunk's last edge)."""
+    from gnnc.b200 import runtime as rt
+
+    n, H = 1700, 4
+    ei = random_graph(n, 25000, 77, heavy=((3, 6000),))
+    rowptr, col, _ = rt.csr_from_coo(ei.to(device), n, self_loops=True, dedupe=False)
+    E = col.numel()
+    g = torch.Generator().manual_seed(77)
+    s = torch.randn(E, H, generator=g)
+    h_host = torch.randn(n, 256, generator=g).to(torch.bfloat16)
+    h = rt.empty_rows(n, 256, torch.bfloat16, device)
+    h.copy_(h_host)
+    out = rt.softmax_aggregate(_plan(rowptr), rowptr, col, s.to(device), h, heads=H)
+    rp, c = rowptr.cpu().long(), col.cpu().long()
+    hd64 = h_host.double()
+    ref = torch.cat([O.softmax_aggregate(rp, c, s[:, k].double(), hd64[:, 64 * k : 64 * k + 64],
+                                         eps=1e-16) for k in range(H)], dim=1)
+    assert_close(out, ref)
+
+
+def test_bad_column_bf16_256_wide(device):
+    from gnnc.b200 import runtime as rt
+    from gnnc.b200._lib import GnncInvalidArgument
+
+    rowptr = torch.tensor([0, 2, 5], dtype=torch.int32, device=device)
+    col = torch.tensor([0, 1, 1, 7, 1 << 30], dtype=torch.int32, device=device)
+    h = torch.ones(4, 256, device=device).to(torch.bfloat16)
+    asrc = torch.zeros(4, 4, device=device)
+    adst = torch.zeros(2, 4, device=device)
+    out = rt.gat_aggregate(_plan(rowptr), rowptr, col, h, asrc, adst, heads=4)
+    with pytest.raises(GnncInvalidArgument):
+        rt.Context.get(device).synchronize()
+    # the bad edges are dropped: row 1 keeps its one in-range edge
+    assert torch.allclose(out.cpu(), torch.ones(2, 256))
