@@ -135,6 +135,27 @@ __device__ __forceinline__ float out_value(const AggParams& p, const float* s_ro
 // (already normalised) [F] values.
 __device__ void warp_epilogue(const AggParams& p, int64_t row, const float* s_row, int lane) {
   const int Fo = p.F_out;
+  if (Fo <= 64) {
+    // At most two columns per lane: each output value is formed once and kept
+    // in registers (same values and summation order as the loop below).
+    const int c0 = lane, c1 = lane + 32;
+    const bool ok0 = c0 < Fo, ok1 = c1 < Fo;
+    float v0 = ok0 ? out_value(p, s_row, c0) : -INFINITY;
+    float v1 = ok1 ? out_value(p, s_row, c1) : -INFINITY;
+    if (p.log_softmax) {
+      const float m = warp_max(fmaxf(v0, v1));
+      float se = 0.f;
+      if (ok0) se += expf(v0 - m);
+      if (ok1) se += expf(v1 - m);
+      const float l = logf(warp_sum(se));
+      v0 = (v0 - m) - l;
+      v1 = (v1 - m) - l;
+    }
+    const size_t base = size_t(row) * size_t(p.ldo);
+    if (ok0) store_val(p.out, p.out_dtype, base + c0, v0);
+    if (ok1) store_val(p.out, p.out_dtype, base + c1, v1);
+    return;
+  }
   float mx = 0.f, lse = 0.f;
   if (p.log_softmax) {
     float m = -INFINITY;
@@ -521,6 +542,101 @@ struct AggFast {
   }
 };
 
+// Edge loop specialised for narrow bf16 rows (32 < F <= 64: one 16-byte load
+// per lane, four edges side by side in 8-lane groups) and a compile-time head
+// count KH (0: GCN edge weights). The scores are formed as in AggFast; each
+// group then takes every fourth edge of the chunk, eight at a time with
+// predicated loads, so a partial chunk costs no loop control. Same arithmetic
+// per edge, in the same order within a group, as Agg<bf16, 8, 8, 1>::range.
+template <int KH>
+struct AggNarrow {
+  static constexpr int HS = KH == 0 ? 1 : (KH | 1);
+
+  static __device__ __forceinline__ void range(const AggParams& p, int64_t row, int eb, int ee,
+                                               float (&acc)[1][8], float (&s_acc)[1],
+                                               float& m_reg, int32_t* s_col, float* s_p,
+                                               const int (&hv)[1], int lane) {
+    const int lig = lane & 7;
+    const int grp = lane >> 3;
+    const bool vok = lig * 8 < p.F;
+    const char* hlane = reinterpret_cast<const char*>(p.h) + lig * 16;
+    const uint32_t ldh_b = uint32_t(p.ldh) * 2u;
+    const float* s_ph = s_p + hv[0];
+    float sc_reg = 1.f;
+    float ad_reg = 0.f;
+    if (KH > 0 && p.mode == MODE_GAT && lane < KH) ad_reg = __ldg(p.adst + size_t(row) * KH + lane);
+    for (int cb = eb; cb < ee; cb += 32) {
+      const int k = cb + lane;
+      bool valid = k < ee;
+      int src = valid ? __ldg(p.col + k) : 0;
+      if (valid && unsigned(src) >= unsigned(p.n_src)) {
+        atomicOr(p.counters + 2, 1);
+        valid = false;
+        src = 0;
+      }
+      s_col[lane] = src;
+      if constexpr (KH == 0) {
+        s_p[lane] = valid ? __ldg(p.w + k) : 0.f;
+      } else {
+        const float* xs = p.mode == MODE_GAT ? p.asrc + size_t(src) * KH
+                                             : p.scores + size_t(valid ? k : cb) * KH;
+        bool rescale = false;
+#pragma unroll
+        for (int hd = 0; hd < KH; ++hd) {
+          const float ad = __shfl_sync(kFull, ad_reg, hd);
+          float e = -INFINITY;
+          if (valid) {
+            const float x = __ldg(xs + hd);
+            if (p.mode == MODE_GAT) {
+              const float t = x + ad;
+              e = t > 0.f ? t : t * p.slope;
+            } else {
+              e = x;
+            }
+          }
+          const float cmax = warp_max_redux(e);
+          const float m_old = __shfl_sync(kFull, m_reg, hd);
+          const float m_new = fmaxf(m_old, cmax);
+          const float pr = valid ? __expf(e - m_new) : 0.f;
+          const float sc = __expf(m_old - m_new);
+          if (lane == hd) {
+            sc_reg = sc;
+            m_reg = m_new;
+          }
+          rescale |= (cb != eb) && (m_new != m_old);
+          s_p[lane * HS + hd] = pr;
+        }
+        if (rescale) {  // warp-uniform
+          const float sc = __shfl_sync(kFull, sc_reg, hv[0]);
+          s_acc[0] *= sc;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[0][e] *= sc;
+        }
+      }
+      __syncwarp();
+      const int n = min(32, ee - cb);
+      uint4 v[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const int j = grp + 4 * t;
+        v[t] = make_uint4(0u, 0u, 0u, 0u);
+        if (vok && j < n)
+          v[t] = __ldg(reinterpret_cast<const uint4*>(hlane + size_t(uint32_t(s_col[j])) * ldh_b));
+      }
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const int j = grp + 4 * t;
+        if (j < n) {
+          const float a = s_ph[j * HS];
+          s_acc[0] += a;
+          AggFast<KH>::fma_row(acc[0], a, v[t]);
+        }
+      }
+      __syncwarp();
+    }
+  }
+};
+
 // Selects the edge loop: the specialised one for KH >= 0, the generic otherwise.
 template <typename TH, int VEC, int LPG, int NV, int KH>
 struct EdgeLoop {
@@ -533,6 +649,14 @@ struct EdgeLoop<__nv_bfloat16, 8, 32, 1, KH> {
 template <>
 struct EdgeLoop<__nv_bfloat16, 8, 32, 1, -1> {
   using type = Agg<__nv_bfloat16, 8, 32, 1>;
+};
+template <int KH>
+struct EdgeLoop<__nv_bfloat16, 8, 8, 1, KH> {
+  using type = AggNarrow<KH>;
+};
+template <>
+struct EdgeLoop<__nv_bfloat16, 8, 8, 1, -1> {
+  using type = Agg<__nv_bfloat16, 8, 8, 1>;
 };
 
 template <typename TH, int VEC, int LPG, int NV, int KH = -1>
@@ -803,7 +927,18 @@ int run_aggregate(gnnc_ctx_t* ctx, const Launch& L, AggParams p) {
                            "feature width %d too large for the row kernel (vector width %d)", p.F,
                            vec);
   KernelFn fn = nullptr;
-  if (L.h_dtype == GNNC_BF16 && vec == 8 && p.F == 256) {
+  if (L.h_dtype == GNNC_BF16 && vec == 8 && lpg == 8 && nv == 1) {
+    // Narrow rows (32 < F <= 64): specialised loop for a compile-time head count.
+    switch (p.mode == MODE_GCN ? 0 : p.H) {
+      case 0: fn = agg_kernel<__nv_bfloat16, 8, 8, 1, 0>; break;
+      case 1: fn = agg_kernel<__nv_bfloat16, 8, 8, 1, 1>; break;
+      case 2: fn = agg_kernel<__nv_bfloat16, 8, 8, 1, 2>; break;
+      case 4: fn = agg_kernel<__nv_bfloat16, 8, 8, 1, 4>; break;
+      case 8: fn = agg_kernel<__nv_bfloat16, 8, 8, 1, 8>; break;
+      default: break;
+    }
+  }
+  if (!fn && L.h_dtype == GNNC_BF16 && vec == 8 && p.F == 256) {
     // Specialised edge loop for a compile-time head count. It reads a_src
     // rows (or score rows) as one vector: they must be aligned to it.
     const int kh = p.mode == MODE_GCN ? 0 : p.H;

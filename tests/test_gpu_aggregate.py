@@ -252,3 +252,39 @@ def test_bad_column_bf16_256_wide(device):
         rt.Context.get(device).synchronize()
     # the bad edges are dropped: row 1 keeps its one in-range edge
     assert torch.allclose(out.cpu(), torch.ones(2, 256))
+
+
+@pytest.mark.parametrize("H,C,concat,act,lsm", [(1, 47, False, 0, True), (8, 8, True, 2, False),
+                                                (2, 24, False, 1, False), (4, 16, True, 0, True),
+                                                (1, 40, True, 2, True)])
+def test_gat_bf16_narrow_rows(device, H, C, concat, act, lsm):
+    """bf16 rows of 33-64 features (four edges side by side per warp), every
+    compile-time head count, both head reductions and the log_softmax epilogue
+    (the last c4 layer is 1 x 47, mean, log_softmax)."""
+    out, ref, _ = _gat_case(device, 1800, 30000, H, C, torch.bfloat16, ((4, 7000), (6, 900)), 0,
+                            0, concat, act=act, lsm=lsm, seed=60 + H * C)
+    assert_close(out, ref)
+
+
+@pytest.mark.parametrize("F,lsm", [(47, True), (64, False), (40, False)])
+def test_gcn_bf16_narrow_rows(device, F, lsm):
+    out, ref = _gcn_case(device, 2500, 30000, F, torch.bfloat16, ((5, 9000), (9, 300)), 0, 0,
+                         act=0 if lsm else 1, lsm=lsm, seed=F)
+    assert_close(out, ref)
+
+
+def test_softmax_aggregate_bf16_narrow(device):
+    from gnnc.b200 import runtime as rt
+
+    n = 1200
+    ei = random_graph(n, 15000, 91, heavy=((2, 5000),))
+    rowptr, col, _ = rt.csr_from_coo(ei.to(device), n, self_loops=True, dedupe=False)
+    g = torch.Generator().manual_seed(91)
+    s = torch.randn(col.numel(), generator=g)
+    h_host = torch.randn(n, 48, generator=g).to(torch.bfloat16)
+    h = rt.empty_rows(n, 48, torch.bfloat16, device)
+    h.copy_(h_host)
+    out = rt.softmax_aggregate(_plan(rowptr), rowptr, col, s.to(device), h, heads=1)
+    ref = O.softmax_aggregate(rowptr.cpu().long(), col.cpu().long(), s.double(), h_host.double(),
+                              eps=1e-16)
+    assert_close(out, ref)
