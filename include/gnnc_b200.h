@@ -127,6 +127,15 @@ GNNC_API int gnnc_gcn_norm(gnnc_ctx_t* ctx, const int32_t* rowptr, const int32_t
 /* Checks rowptr[0] >= 0, rowptr non-decreasing, rowptr[n_rows] <= E and
  * every col in [0, n_src). Returns GNNC_ERR_BOUNDS (with the first bad
  * position in the error text) when not. Synchronous. */
+/* Mean-aggregation weights of SAGEConv on a CSR adjacency:
+ *   w_out[k] = w_in[k] / max(#{j in row(k) : w_in[j] != 0}, 1)
+ * (w_in NULL: unit weights, every stored edge counted). Restates the
+ * `_sparse_mm.reduce("mean")` rewrite (A.X) / clamp_min(row_nnz, 1)
+ * (gnnc/conversion/tm_tensor_to_torch/despecialize_sparse_mm_reduce.py:1-75)
+ * as weights on the edges, so gnnc_sage_aggregate is a weighted SpMM. */
+GNNC_API int gnnc_mean_norm(gnnc_ctx_t* ctx, const int32_t* rowptr, int64_t n_rows,
+                            const float* w_in, float* w_out);
+
 GNNC_API int gnnc_csr_validate(gnnc_ctx_t* ctx, const int32_t* rowptr, const int32_t* col,
                       int64_t n_rows, int64_t E, int64_t n_src);
 
@@ -192,6 +201,18 @@ GNNC_API int gnnc_gcn_aggregate(gnnc_ctx_t* ctx, const gnnc_plan_t* plan, const 
                        const int32_t* col, const float* w, const void* h, int h_dtype,
                        int64_t ldh, int64_t n_rows, int64_t n_src, int64_t F, const float* bias,
                        int act, int log_softmax, void* out, int out_dtype, int64_t ldo);
+
+/* SAGEConv (mean aggregation, root weight) after its two projections
+ * h = x.W_l^T and root = x.W_r^T:  out = A_mean.h + root + bias, then act /
+ * log_softmax. w holds gnnc_mean_norm weights. Replaces the SAGE layer of
+ * test/reference/sage.raw.mlir:5-14 (_sparse_mm.reduce "mean", linear with
+ * bias, linear without bias, add, relu); root [n_rows, F] row stride ldr,
+ * dtype root_dtype, indexed like out. */
+GNNC_API int gnnc_sage_aggregate(gnnc_ctx_t* ctx, const gnnc_plan_t* plan, const int32_t* rowptr,
+                        const int32_t* col, const float* w, const void* h, int h_dtype,
+                        int64_t ldh, const void* root, int root_dtype, int64_t ldr,
+                        int64_t n_rows, int64_t n_src, int64_t F, const float* bias, int act,
+                        int log_softmax, void* out, int out_dtype, int64_t ldo);
 
 /* One fused GATConv layer after the projection:
  *   e_k   = LeakyReLU_slope(asrc[src_k,hd] + adst[row,hd])

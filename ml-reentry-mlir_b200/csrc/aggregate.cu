@@ -75,7 +75,15 @@ struct AggParams {
   float* partials;
   int part_stride;
   int* counters;  // [0] next CTA item, [1] next warp task, [2] bad-index flag
+  const void* root;  // SAGE root term [n_rows, F_out] added before bias (null: none)
+  int root_dtype;
+  int64_t ldr;
 };
+
+__device__ __forceinline__ float load_val(const void* base, int dtype, size_t idx) {
+  return dtype == GNNC_BF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[idx])
+                            : reinterpret_cast<const float*>(base)[idx];
+}
 
 template <typename TH, int VEC>
 struct VecLoad;
@@ -118,7 +126,8 @@ __device__ __forceinline__ float apply_act(float v, int act) {
 }
 
 // Final value of output feature c from the aggregated [H*C] row in smem.
-__device__ __forceinline__ float out_value(const AggParams& p, const float* s_row, int c) {
+__device__ __forceinline__ float out_value(const AggParams& p, int64_t row, const float* s_row,
+                                           int c) {
   float v;
   if (p.concat) {
     v = s_row[c];
@@ -127,6 +136,7 @@ __device__ __forceinline__ float out_value(const AggParams& p, const float* s_ro
     for (int hd = 0; hd < p.H; ++hd) v += s_row[hd * p.C + c];
     v = v / float(p.H);
   }
+  if (p.root) v += load_val(p.root, p.root_dtype, size_t(row) * size_t(p.ldr) + c);
   if (p.bias) v += __ldg(p.bias + c);
   return apply_act(v, p.act);
 }
@@ -140,8 +150,8 @@ __device__ void warp_epilogue(const AggParams& p, int64_t row, const float* s_ro
     // in registers (same values and summation order as the loop below).
     const int c0 = lane, c1 = lane + 32;
     const bool ok0 = c0 < Fo, ok1 = c1 < Fo;
-    float v0 = ok0 ? out_value(p, s_row, c0) : -INFINITY;
-    float v1 = ok1 ? out_value(p, s_row, c1) : -INFINITY;
+    float v0 = ok0 ? out_value(p, row, s_row, c0) : -INFINITY;
+    float v1 = ok1 ? out_value(p, row, s_row, c1) : -INFINITY;
     if (p.log_softmax) {
       const float m = warp_max(fmaxf(v0, v1));
       float se = 0.f;
@@ -159,15 +169,15 @@ __device__ void warp_epilogue(const AggParams& p, int64_t row, const float* s_ro
   float mx = 0.f, lse = 0.f;
   if (p.log_softmax) {
     float m = -INFINITY;
-    for (int c = lane; c < Fo; c += 32) m = fmaxf(m, out_value(p, s_row, c));
+    for (int c = lane; c < Fo; c += 32) m = fmaxf(m, out_value(p, row, s_row, c));
     mx = warp_max(m);
     float se = 0.f;
-    for (int c = lane; c < Fo; c += 32) se += expf(out_value(p, s_row, c) - mx);
+    for (int c = lane; c < Fo; c += 32) se += expf(out_value(p, row, s_row, c) - mx);
     lse = logf(warp_sum(se));
   }
   const size_t base = size_t(row) * size_t(p.ldo);
   for (int c = lane; c < Fo; c += 32) {
-    float v = out_value(p, s_row, c);
+    float v = out_value(p, row, s_row, c);
     if (p.log_softmax) v = (v - mx) - lse;
     store_val(p.out, p.out_dtype, base + c, v);
   }
@@ -397,6 +407,12 @@ struct Agg {
       float o[VEC];
 #pragma unroll
       for (int e = 0; e < VEC; ++e) o[e] = acc[v][e] * inv[v];
+      if (p.root) {
+        const size_t rb = size_t(row) * size_t(p.ldr) + e0;
+#pragma unroll
+        for (int e = 0; e < VEC; ++e)
+          if (e0 + e < p.F) o[e] += load_val(p.root, p.root_dtype, rb + e);
+      }
       if (p.bias) {
         if constexpr (VEC % 4 == 0) {
 #pragma unroll
@@ -1184,6 +1200,31 @@ extern "C" int gnnc_gcn_aggregate(gnnc_ctx_t* ctx, const gnnc_plan_t* plan,
   p.H = 1; p.C = int(F); p.F = int(F); p.F_out = int(F);
   p.mode = MODE_GCN; p.concat = 1; p.act = act; p.log_softmax = log_softmax;
   p.bias = bias; p.out = out; p.out_dtype = out_dtype; p.ldo = ldo; p.eps = 0.f;
+  return run_aggregate(ctx, Launch{plan, h, h_dtype, ldh}, p);
+}
+
+extern "C" int gnnc_sage_aggregate(gnnc_ctx_t* ctx, const gnnc_plan_t* plan,
+                                   const int32_t* rowptr, const int32_t* col, const float* w,
+                                   const void* h, int h_dtype, int64_t ldh, const void* root,
+                                   int root_dtype, int64_t ldr, int64_t n_rows, int64_t n_src,
+                                   int64_t F, const float* bias, int act, int log_softmax,
+                                   void* out, int out_dtype, int64_t ldo) {
+  if (!ctx) return GNNC_ERR_INVALID;
+  int st = check_common(ctx, plan, rowptr, col, h, h_dtype, ldh, n_rows, n_src, F, act, out,
+                        out_dtype, ldo, F);
+  if (st) return st;
+  GNNC_CHECK_ARG(ctx, root != nullptr || n_rows == 0, "null root");
+  GNNC_CHECK_ARG(ctx, root_dtype == GNNC_F32 || root_dtype == GNNC_BF16, "bad root dtype");
+  GNNC_CHECK_ARG(ctx, ldr >= F, "ldr (%lld) < F (%lld)", (long long)ldr, (long long)F);
+  if (n_rows == 0) return GNNC_OK;
+  GNNC_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  AggParams p = base_params(plan);
+  p.rowptr = rowptr; p.col = col; p.w = w; p.h = h; p.ldh = ldh;
+  p.n_rows = n_rows; p.n_src = n_src;
+  p.H = 1; p.C = int(F); p.F = int(F); p.F_out = int(F);
+  p.mode = MODE_GCN; p.concat = 1; p.act = act; p.log_softmax = log_softmax;
+  p.bias = bias; p.out = out; p.out_dtype = out_dtype; p.ldo = ldo; p.eps = 0.f;
+  p.root = root; p.root_dtype = root_dtype; p.ldr = ldr;
   return run_aggregate(ctx, Launch{plan, h, h_dtype, ldh}, p);
 }
 

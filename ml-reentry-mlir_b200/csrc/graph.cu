@@ -292,6 +292,25 @@ __global__ void gcn_w_kernel(const int32_t* rowptr, const int32_t* col, const in
   }
 }
 
+// SAGE mean weights: w_out[k] = w_in[k] / max(#{j in row : w_in[j] != 0}, 1)
+// (w_in null: every stored edge counts, weight 1). One warp per row.
+__global__ void mean_w_kernel(const int32_t* rowptr, int64_t n_rows, const float* w_in,
+                              float* w_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x / 32);
+  for (int64_t r = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) / 32; r < n_rows; r += warps) {
+    const int b = rowptr[r], e = rowptr[r + 1];
+    int nnz = 0;
+    for (int k0 = b; k0 < e; k0 += 32) {
+      const int k = k0 + lane;
+      const bool nz = k < e && (w_in == nullptr || w_in[k] != 0.f);
+      nnz += __popc(__ballot_sync(0xffffffffu, nz));
+    }
+    const float d = float(nnz > 1 ? nnz : 1);
+    for (int k = b + lane; k < e; k += 32) w_out[k] = __fdiv_rn(w_in ? w_in[k] : 1.f, d);
+  }
+}
+
 __global__ void validate_kernel(const int32_t* rowptr, const int32_t* col, int64_t n_rows,
                                 int64_t E, int64_t n_src, int* words) {
   const int64_t stride = int64_t(gridDim.x) * blockDim.x;
@@ -448,6 +467,19 @@ extern "C" int gnnc_gcn_norm(gnnc_ctx_t* ctx, const int32_t* rowptr, const int32
                                                                           di);
   gcn_w_kernel<<<grid_for(N * 32, 256, ctx->num_sms), 256, 0, ctx->stream>>>(rowptr, col, mult,
                                                                              N, di, w);
+  GNNC_CUDA_TRY(ctx, cudaGetLastError());
+  return GNNC_OK;
+}
+
+extern "C" int gnnc_mean_norm(gnnc_ctx_t* ctx, const int32_t* rowptr, int64_t n_rows,
+                              const float* w_in, float* w_out) {
+  if (!ctx) return GNNC_ERR_INVALID;
+  GNNC_CHECK_ARG(ctx, n_rows >= 0, "negative n_rows");
+  GNNC_CHECK_ARG(ctx, n_rows == 0 || (rowptr && w_out), "null rowptr/w_out");
+  if (n_rows == 0) return GNNC_OK;
+  GNNC_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  mean_w_kernel<<<grid_for(n_rows * 32, 256, ctx->num_sms), 256, 0, ctx->stream>>>(
+      rowptr, n_rows, w_in, w_out);
   GNNC_CUDA_TRY(ctx, cudaGetLastError());
   return GNNC_OK;
 }

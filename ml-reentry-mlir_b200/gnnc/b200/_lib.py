@@ -69,6 +69,12 @@ SIGNATURES: dict[str, tuple] = {
             _P, c_int, c_int, _P, c_int, _I64,
         ],
     ),
+    "gnnc_mean_norm": (c_int, [_P, _P, _I64, _P, _P]),
+    "gnnc_sage_aggregate": (
+        c_int,
+        [_P, _P, _P, _P, _P, _P, c_int, _I64, _P, c_int, _I64, _I64, _I64, _I64, _P, c_int,
+         c_int, _P, c_int, _I64],
+    ),
     "gnnc_peer_export": (c_int, [_P, _P, _P, POINTER(ctypes.c_uint64)]),
     "gnnc_peer_open": (c_int, [_P, _P, ctypes.c_uint64, POINTER(c_void_p)]),
     "gnnc_peer_close": (c_int, [_P, _P, ctypes.c_uint64]),

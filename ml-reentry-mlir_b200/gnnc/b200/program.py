@@ -4,14 +4,18 @@ The reference lowers a PyG model through torch.export, torch-mlir and the MLIR
 sparsifier (gnnc/compile.py:109-124, gnnc/schedule/sparse.py:21-114); its
 aggregation reaches the backend as aten._sparse_mm (test/reference/gcn.raw.mlir:7).
 The B200 target instead traces the model with torch.fx, keeping GCNConv /
-GATConv modules as leaves, and matches the chain
+GATConv / SAGEConv modules as leaves, and matches the chain
 
     x -> conv -> [relu | elu] -> [dropout(eval)] -> conv -> ... -> [log_softmax]
 
 into one LayerOp per conv. Each LayerOp becomes two kernel launches: the dense
 projection (gnnc_proj, with GAT's attention coefficients in its epilogue) and
 the aggregation (gnnc_gcn_aggregate / gnnc_gat_aggregate) with bias, the
-activation and the final log_softmax fused into its epilogue.
+activation and the final log_softmax fused into its epilogue. A SAGEConv layer
+projects twice (lin_l for the neighbours, lin_r for the root) and aggregates
+with gnnc_sage_aggregate on mean-normalised edge weights (the reference's
+`_sparse_mm.reduce("mean")`, test/reference/sage.raw.mlir:5), adding the root
+term in the epilogue.
 """
 
 from __future__ import annotations
@@ -26,7 +30,7 @@ import torch.nn.functional as F
 
 from gnnc.b200 import runtime as rt
 
-_CONV_CLASSES = ("GCNConv", "GATConv")
+_CONV_CLASSES = ("GCNConv", "GATConv", "SAGEConv")
 
 
 def _is_conv(mod: torch.nn.Module) -> bool:
@@ -39,7 +43,7 @@ class _Tracer(fx.Tracer):
 
 
 def trace(model: torch.nn.Module) -> fx.GraphModule:
-    """fx graph of `model` with GCNConv / GATConv kept as call_module leaves."""
+    """fx graph of `model` with GCNConv / GATConv / SAGEConv kept as call_module leaves."""
     model.eval()
     graph = _Tracer().trace(model)
     return fx.GraphModule(model, graph)
@@ -62,6 +66,7 @@ class LayerOp:
     bias: torch.Tensor | None
     act: int = rt.ACT_NONE
     log_softmax: bool = False
+    weight_root: torch.Tensor | None = None  # SAGE lin_r [F, in]
 
     @property
     def width(self) -> int:
@@ -80,6 +85,10 @@ class LayerOp:
                 f"gnnc_gat_aggregate heads={self.heads} C={self.channels} "
                 f"slope={self.negative_slope} concat={int(self.concat)}"
             )
+        elif self.kind == "sage":
+            proj = (f"gnnc_proj [{self.in_channels} -> {self.width}] (lin_l) and "
+                    f"[{self.in_channels} -> {self.width}] (lin_r, root)")
+            agg = f"gnnc_sage_aggregate F={self.width} mean weights (gnnc_mean_norm) + root"
         else:
             agg = f"gnnc_gcn_aggregate F={self.width} normalize={int(self.normalize)}"
         epi = f"bias={'yes' if self.bias is not None else 'no'} act={act}"
@@ -115,6 +124,22 @@ def _layer_from_module(name: str, mod: torch.nn.Module) -> LayerOp:
             add_self_loops=bool(getattr(mod, "add_self_loops", True)), weight=w,
             att_src=None, att_dst=None,
             bias=None if mod.bias is None else mod.bias.detach(),
+        )
+    if cls == "SAGEConv":
+        aggr = getattr(mod, "aggr", "mean")
+        if str(aggr).lower() not in ("mean", "meanaggregation()"):
+            raise NotImplementedError(f"{name}: SAGEConv(aggr={aggr!r}) is not supported (mean only)")
+        if getattr(mod, "normalize", False) or getattr(mod, "project", False):
+            raise NotImplementedError(f"{name}: SAGEConv(normalize/project) is not supported")
+        if not getattr(mod, "root_weight", True):
+            raise NotImplementedError(f"{name}: SAGEConv(root_weight=False) is not supported")
+        wl = mod.lin_l.weight.detach()
+        return LayerOp(
+            name=name, kind="sage", in_channels=wl.size(1), heads=1, channels=wl.size(0),
+            concat=True, negative_slope=0.0, normalize=False, add_self_loops=False, weight=wl,
+            att_src=None, att_dst=None,
+            bias=None if mod.lin_l.bias is None else mod.lin_l.bias.detach(),
+            weight_root=mod.lin_r.weight.detach(),
         )
     # GATConv: PyG >= 2.5 names the shared projection `lin`; older releases `lin_src`.
     lin = getattr(mod, "lin", None)
@@ -154,7 +179,7 @@ def lower_graph(gm: fx.GraphModule, feature_dtype: torch.dtype | None = None,
     def expect_current(node: fx.Node, arg) -> None:
         if arg is not current:
             raise NotImplementedError(
-                f"{node.format_node()}: only a linear chain of GCNConv/GATConv layers is supported"
+                f"{node.format_node()}: only a linear chain of GCNConv/GATConv/SAGEConv layers is supported"
             )
 
     def act_of(node: fx.Node) -> int | None:
@@ -235,7 +260,7 @@ def lower_graph(gm: fx.GraphModule, feature_dtype: torch.dtype | None = None,
         raise NotImplementedError(f"op {node.format_node()} is not supported by the b200 target")
 
     if not layers:
-        raise NotImplementedError("no GCNConv/GATConv layer found")
+        raise NotImplementedError("no GCNConv/GATConv/SAGEConv layer found")
     for prev, nxt in zip(layers, layers[1:], strict=False):
         if prev.out_width != nxt.in_channels:
             raise ValueError(f"{nxt.name} expects {nxt.in_channels} features, gets {prev.out_width}")
@@ -363,6 +388,7 @@ class B200Executable:
         )
         dt = program.feature_dtype
         self._weights = []
+        self._roots: list[torch.Tensor | None] = []
         for layer in program.layers:
             w = layer.weight.to(device=self.device, dtype=dt)
             w = to_device_features(w, dt, self.device)
@@ -372,6 +398,11 @@ class B200Executable:
                 adst = layer.att_dst.to(self.device, torch.float32).contiguous()
             bias = None if layer.bias is None else layer.bias.to(self.device, torch.float32)
             self._weights.append((w, asrc, adst, bias))
+            wr = None
+            if layer.weight_root is not None:
+                wr = to_device_features(layer.weight_root.to(device=self.device, dtype=dt), dt,
+                                        self.device)
+            self._roots.append(wr)
         self._graphs: dict[tuple, tuple[object, DeviceGraph]] = {}
         self._results = _PinnedResults()
         self._copy_stream: torch.cuda.Stream | None = None
@@ -394,14 +425,19 @@ class B200Executable:
 
     def _graph_for(self, graph: torch.Tensor, num_nodes: int, layer: LayerOp) -> DeviceGraph:
         if graph.layout == torch.sparse_csr:
-            if layer.kind != "gcn" or layer.normalize:
+            if layer.kind == "sage":
+                mode = ("csr-mean",)
+            elif layer.kind != "gcn" or layer.normalize:
                 raise NotImplementedError(
                     "a sparse CSR adjacency must be pre-normalised for GCNConv(normalize=False)"
                 )
-            mode = ("csr",)
+            else:
+                mode = ("csr",)
         elif graph.layout == torch.strided:
             if layer.kind == "gcn":
                 mode = ("coo", layer.add_self_loops, True, layer.normalize)
+            elif layer.kind == "sage":
+                mode = ("coo-mean",)
             else:
                 mode = ("coo", layer.add_self_loops, False, False)
         else:
@@ -412,6 +448,14 @@ class B200Executable:
             return hit[1]
         if mode[0] == "csr":
             g = graph_from_csr(graph, self.device)
+        elif mode[0] == "csr-mean":
+            g = graph_from_csr(graph, self.device)
+            g.w = rt.mean_norm(g.rowptr, g.w)
+        elif mode[0] == "coo-mean":
+            # SAGEConv on an edge list: no self-loops added, duplicates counted
+            g = graph_from_edge_index(graph, num_nodes, self.device, self_loops=False,
+                                      dedupe=False, normalize=False)
+            g.w = rt.mean_norm(g.rowptr)
         else:
             g = graph_from_edge_index(
                 graph, num_nodes, self.device, self_loops=mode[1], dedupe=mode[2], normalize=mode[3]
@@ -443,7 +487,9 @@ class B200Executable:
         h_in = to_device_features(x, dt, self.device)
         layers = self.program.layers
         with torch.cuda.device(self.device):
-            for i, (layer, (w, asrc_w, adst_w, bias)) in enumerate(zip(layers, self._weights, strict=True)):
+            for i, (layer, (w, asrc_w, adst_w, bias), wr) in enumerate(
+                zip(layers, self._weights, self._roots, strict=True)
+            ):
                 g = self._graph_for(graph, n, layer)
                 ev = None
                 if events is not None:
@@ -452,8 +498,14 @@ class B200Executable:
                     events.append(ev)
                 last = i == len(layers) - 1
                 out_dtype = self.program.output_dtype if last else dt
+                root = None
                 if layer.kind == "gcn":
                     h = rt.proj(h_in, w, out_dtype=dt)
+                    asrc = adst = None
+                    width = h.size(1)
+                elif layer.kind == "sage":
+                    h = rt.proj(h_in, w, out_dtype=dt)
+                    root = rt.proj(h_in, wr, out_dtype=dt)
                     asrc = adst = None
                     width = h.size(1)
                 else:
@@ -465,20 +517,23 @@ class B200Executable:
                 out = rt.empty_rows(n, width, out_dtype, self.device)
                 if last and host_out is not None:
                     host = host_out((n, width), out_dtype)
-                    self._aggregate_to_host(layer, g, h, asrc, adst, bias, out, host)
+                    self._aggregate_to_host(layer, g, h, asrc, adst, bias, out, host, root)
                     h_in = host
                 else:
-                    self._aggregate(layer, g, g.plan, 0, n, h, asrc, adst, bias, out)
+                    self._aggregate(layer, g, g.plan, 0, n, h, asrc, adst, bias, out, root)
                     h_in = out
                 if ev:
                     ev[2].record()
         return h_in
 
     @staticmethod
-    def _aggregate(layer, g, plan, r0, r1, h, asrc, adst, bias, out) -> None:
+    def _aggregate(layer, g, plan, r0, r1, h, asrc, adst, bias, out, root=None) -> None:
         """Aggregate destination rows [r0, r1) (plan covers exactly those rows)."""
         rowptr = g.rowptr[r0 : r1 + 1]
-        if layer.kind == "gcn":
+        if layer.kind == "sage":
+            rt.sage_aggregate(plan, rowptr, g.col, g.w, h, root[r0:r1], bias=bias, act=layer.act,
+                              log_softmax=layer.log_softmax, out_dtype=out.dtype, out=out[r0:r1])
+        elif layer.kind == "gcn":
             rt.gcn_aggregate(plan, rowptr, g.col, g.w, h, bias=bias, act=layer.act,
                              log_softmax=layer.log_softmax, out_dtype=out.dtype,
                              out=out[r0:r1], n_src=h.size(0))
@@ -488,7 +543,7 @@ class B200Executable:
                              bias=bias, act=layer.act, log_softmax=layer.log_softmax,
                              out_dtype=out.dtype, out=out[r0:r1])
 
-    def _aggregate_to_host(self, layer, g, h, asrc, adst, bias, out, host) -> None:
+    def _aggregate_to_host(self, layer, g, h, asrc, adst, bias, out, host, root=None) -> None:
         k = self.host_chunks if g.num_edges >= self.host_chunks * self.host_chunk_min_edges else 1
         cur = torch.cuda.current_stream(self.device)
         if self._copy_stream is None:
@@ -496,7 +551,7 @@ class B200Executable:
         side = self._copy_stream
         chunks = g.row_chunks(k) if k > 1 else [(0, g.num_nodes, g.plan)]
         for r0, r1, plan in chunks:
-            self._aggregate(layer, g, plan, r0, r1, h, asrc, adst, bias, out)
+            self._aggregate(layer, g, plan, r0, r1, h, asrc, adst, bias, out, root)
             done = torch.cuda.Event()
             done.record(cur)
             side.wait_event(done)

@@ -32,11 +32,13 @@ __all__ = [
     "gat_aggregate_noalloc",
     "gcn_aggregate",
     "gcn_norm",
+    "mean_norm",
     "peer_close",
     "peer_copy",
     "peer_export",
     "peer_open",
     "proj",
+    "sage_aggregate",
     "softmax_aggregate",
     "validate_csr",
 ]
@@ -389,6 +391,56 @@ def gcn_aggregate(
         "gnnc_gcn_aggregate",
         plan.handle, rowptr.data_ptr(), col.data_ptr(), w.data_ptr(), h.data_ptr(), _dt(h),
         _ld(h), n_rows, h.size(0) if n_src is None else n_src, F, _p(bias), act,
+        int(log_softmax), out.data_ptr(), _dt(out), _ld(out),
+    )
+    return out
+
+
+def mean_norm(rowptr: torch.Tensor, w: torch.Tensor | None = None) -> torch.Tensor:
+    """SAGE mean weights: w / max(count of nonzero w in the row, 1) (w None: unit weights)."""
+    _check_cuda(rowptr, w)
+    n_rows = rowptr.numel() - 1
+    E = int(rowptr[-1].item()) if n_rows >= 0 else 0
+    if w is not None:
+        w = w.to(torch.float32).contiguous()
+        if w.numel() < E:
+            raise ValueError(f"w has {w.numel()} entries, the CSR needs {E}")
+    out = torch.empty(max(E, w.numel() if w is not None else 0), dtype=torch.float32,
+                      device=rowptr.device)
+    Context.get(rowptr.device).call("gnnc_mean_norm", rowptr.data_ptr(), n_rows, _p(w),
+                                    out.data_ptr())
+    return out
+
+
+def sage_aggregate(
+    plan: Plan,
+    rowptr: torch.Tensor,
+    col: torch.Tensor,
+    w: torch.Tensor,
+    h: torch.Tensor,
+    root: torch.Tensor,
+    *,
+    bias: torch.Tensor | None = None,
+    act: int = ACT_NONE,
+    log_softmax: bool = False,
+    out_dtype: torch.dtype = torch.float32,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """SAGEConv after its projections: out = A_mean . h + root (+bias, act, log_softmax).
+
+    w: mean_norm weights of the CSR; root: [n_rows, F] (x . W_r^T of the rows)."""
+    _check_cuda(rowptr, col, w, h, root, bias)
+    n_rows = rowptr.numel() - 1
+    F = h.size(1)
+    if root.dim() != 2 or root.size(0) != n_rows or root.size(1) != F:
+        raise ValueError(f"root must be [{n_rows}, {F}]")
+    out = _out(n_rows, F, out_dtype, h.device, out)
+    _check_edges(plan, col, w)
+    bias = None if bias is None else bias.to(torch.float32).contiguous()
+    plan.ctx.call(
+        "gnnc_sage_aggregate",
+        plan.handle, rowptr.data_ptr(), col.data_ptr(), w.data_ptr(), h.data_ptr(), _dt(h),
+        _ld(h), root.data_ptr(), _dt(root), _ld(root), n_rows, h.size(0), F, _p(bias), act,
         int(log_softmax), out.data_ptr(), _dt(out), _ld(out),
     )
     return out

@@ -43,17 +43,20 @@ def synthetic_inputs(model_name: str, name: str):
     from gnnc.examples import synthetic as S
     from gnnc.examples.util import normalized_csr_adj
 
+    # GraphSAGE runs on the GCN workloads' graphs and features (the reference
+    # feeds its SAGE model the GCN model's normalised CSR adjacency).
+    graph_model = "gcn" if model_name == "sage" else model_name
     key = name
     if name == "c4":
-        key = f"c4-{model_name}"
+        key = f"c4-{graph_model}"
     if key not in S.CONFIGS:
         raise ValueError(f"unknown dataset: {name}")
     cfg = S.CONFIGS[key]
-    if cfg.model != model_name:
+    if cfg.model != graph_model:
         raise ValueError(f"workload {name} is defined for model {cfg.model!r}, not {model_name!r}")
     ei = S.make_graph(cfg)
     x = S.make_features(cfg)
-    if model_name == "gcn":
+    if graph_model == "gcn":
         graph = normalized_csr_adj(ei, cfg.num_nodes)
         return (x, graph), (cfg.in_channels, cfg.hidden, cfg.out_channels), {"num_layers": cfg.num_layers}
     kw = {"heads": cfg.heads, "num_layers": cfg.num_layers}
@@ -75,5 +78,6 @@ def _dataset_inputs(model_name: str, dataset: str):
 
         ds = PygNodePropPredDataset(name="ogbn-arxiv", root=str(DATA_DIR / "ogb"))
     data = ds[0]
-    graph = normalized_csr_adj(data.edge_index, data.num_nodes) if model_name == "gcn" else data.edge_index
+    graph = (normalized_csr_adj(data.edge_index, data.num_nodes) if model_name in ("gcn", "sage")
+             else data.edge_index)
     return (data.x, graph), (ds.num_node_features, _DEFAULT_HIDDEN, ds.num_classes), {}

@@ -1,4 +1,4 @@
-"""PyG-compatible GCNConv / GATConv layers for environments without torch_geometric.
+"""PyG-compatible GCNConv / GATConv / SAGEConv layers for environments without torch_geometric.
 
 The reference's models are stock PyG layers (gnnc/examples/models/gcn.py:23,36-37;
 experiments/pyg-baseline/run.py:47,78-88). These classes keep PyG's parameter
@@ -8,6 +8,10 @@ weight is glorot-initialised twice (once by Linear's constructor, once by the
 conv's reset_parameters), then att_src, att_dst, then zero bias. The weights
 embedded in test/reference/gcn.raw.mlir and
 experiments/gatconv/dumps/gat.1-raw-torch.mlir:137-139 reproduce bit for bit.
+SAGEConv's lin_l / lin_r use PyG Linear's default initialisation (kaiming
+uniform with a = sqrt(5), bias uniform in +-1/sqrt(fan_in)), drawn once by each
+Linear's constructor and again by the conv's reset_parameters; the weights in
+test/reference/sage.raw.mlir reproduce bit for bit.
 
 `forward` is the eager PyTorch definition of the layer (the semantics
 `gnnc-bench` compares against). The B200 path never calls it:
@@ -23,7 +27,7 @@ import torch
 import torch.nn.functional as F
 from torch import Tensor, nn
 
-__all__ = ["GATConv", "GCNConv", "Linear", "glorot", "gcn_norm_edges"]
+__all__ = ["GATConv", "GCNConv", "Linear", "SAGEConv", "glorot", "gcn_norm_edges", "spmm_mean"]
 
 
 def glorot(t: Tensor | None) -> None:
@@ -42,12 +46,16 @@ def _zeros(t: Tensor | None) -> None:
 
 
 class Linear(nn.Module):
-    """torch_geometric.nn.dense.Linear with weight_initializer='glorot'."""
+    """torch_geometric.nn.dense.Linear: weight_initializer='glorot' (zero bias,
+    as GCNConv / GATConv build it) or None (PyG's default: kaiming uniform,
+    bias uniform in +-1/sqrt(in_channels), as SAGEConv builds it)."""
 
-    def __init__(self, in_channels: int, out_channels: int, bias: bool = True) -> None:
+    def __init__(self, in_channels: int, out_channels: int, bias: bool = True,
+                 weight_initializer: str | None = "glorot") -> None:
         super().__init__()
         self.in_channels = in_channels
         self.out_channels = out_channels
+        self.weight_initializer = weight_initializer
         self.weight = nn.Parameter(torch.empty(out_channels, in_channels))
         if bias:
             self.bias = nn.Parameter(torch.empty(out_channels))
@@ -56,8 +64,17 @@ class Linear(nn.Module):
         self.reset_parameters()
 
     def reset_parameters(self) -> None:
-        glorot(self.weight)
-        _zeros(self.bias)
+        if self.weight_initializer == "glorot":
+            glorot(self.weight)
+            _zeros(self.bias)
+            return
+        # PyG inits.kaiming_uniform(fan=in_channels, a=sqrt(5)) and inits.uniform
+        bound = math.sqrt(6.0 / ((1.0 + 5.0) * self.in_channels))
+        with torch.no_grad():
+            self.weight.uniform_(-bound, bound)
+            if self.bias is not None:
+                b = 1.0 / math.sqrt(self.in_channels)
+                self.bias.uniform_(-b, b)
 
     def forward(self, x: Tensor) -> Tensor:
         return F.linear(x, self.weight, self.bias)
@@ -209,3 +226,55 @@ class GATConv(nn.Module):
         if self.bias is not None:
             out = out + self.bias
         return out
+
+
+def spmm_mean(adj: Tensor, x: Tensor) -> Tensor:
+    """(A . x) / clamp_min(row_nnz, 1) over a sparse CSR adjacency, row_nnz the
+    number of nonzero stored values of the row (the reference's
+    `_sparse_mm.reduce("mean")` rewrite,
+    gnnc/conversion/tm_tensor_to_torch/despecialize_sparse_mm_reduce.py:1-75)."""
+    crow = adj.crow_indices()
+    vals = adj.values()
+    rows = torch.repeat_interleave(torch.arange(crow.numel() - 1, device=x.device), crow.diff())
+    nnz = torch.zeros(crow.numel() - 1, dtype=x.dtype, device=x.device).index_add_(
+        0, rows, (vals != 0).to(x.dtype))
+    return (adj.to(x.dtype) @ x) / nnz.clamp_min(1.0).unsqueeze(1)
+
+
+class SAGEConv(nn.Module):
+    """PyG SAGEConv(in, out) with the defaults (aggr='mean', root_weight=True,
+    normalize=False, project=False, bias=True):
+
+        out = lin_l(mean_{j in N(i)} x_j) + lin_r(x_i)
+
+    On a torch.sparse_csr adjacency the mean is spmm_mean (values used, rows
+    divided by their count of nonzero values), as the reference's SAGE model
+    feeds it (gnnc/examples/models/sage.py; test/reference/sage.raw.mlir:5-14).
+    On an edge_index [2, E] the mean is over incoming edges (duplicates counted)."""
+
+    def __init__(self, in_channels: int, out_channels: int, bias: bool = True) -> None:
+        super().__init__()
+        self.in_channels = in_channels
+        self.out_channels = out_channels
+        self.aggr = "mean"
+        self.root_weight = True
+        self.normalize = False
+        self.lin_l = Linear(in_channels, out_channels, bias=bias, weight_initializer=None)
+        self.lin_r = Linear(in_channels, out_channels, bias=False, weight_initializer=None)
+        self.reset_parameters()
+
+    def reset_parameters(self) -> None:
+        self.lin_l.reset_parameters()
+        self.lin_r.reset_parameters()
+
+    def forward(self, x: Tensor, graph: Tensor) -> Tensor:
+        if graph.layout == torch.sparse_csr:
+            aggr = spmm_mean(graph, x)
+        else:
+            src, dst = graph[0], graph[1]
+            n = x.size(0)
+            deg = torch.zeros(n, dtype=x.dtype, device=x.device).index_add_(
+                0, dst, torch.ones_like(dst, dtype=x.dtype))
+            aggr = torch.zeros_like(x).index_add_(0, dst, x.index_select(0, src))
+            aggr = aggr / deg.clamp_min(1.0).unsqueeze(1)
+        return self.lin_l(aggr) + self.lin_r(x)

@@ -20,6 +20,8 @@ plain PyTorch CPU ops, following the reference's own call sites:
   softmax_aggregate     <- experiments/gat-gpu-codegen/gat-kernel.mlir:31-132
   gat_rows_fp64         <- the same GAT math, chunked over destination rows in
                            float64 for graphs whose E x H x C messages do not fit
+  spmm_mean / sage_layer <- test/reference/sage.raw.mlir:5-27 and the mean rewrite
+                           gnnc/conversion/tm_tensor_to_torch/despecialize_sparse_mm_reduce.py:1-75
 
 Pinning. tests/test_oracle_golden.py checks this oracle against every known
 answer the reference carries for the path: the GCN and GATConv weight blobs
@@ -149,6 +151,39 @@ def gcn_layer(x, crow, col, val, weight, bias=None, act=None, log_softmax=False)
     out = spmm_csr(crow, col, val, h)
     if bias is not None:
         out = out + bias
+    out = _act(out, act)
+    return F.log_softmax(out, dim=-1) if log_softmax else out
+
+
+def spmm_mean(crow, col, val, x):
+    """_sparse_mm.reduce("mean"): (A . x) / clamp_min(row_nnz, 1), row_nnz = the row's
+    count of nonzero values (despecialize_sparse_mm_reduce.py:1-75)."""
+    crow = torch.as_tensor(crow, dtype=torch.int64)
+    val = torch.as_tensor(val, dtype=x.dtype)
+    rows = torch.repeat_interleave(torch.arange(crow.numel() - 1), crow.diff())
+    nnz = x.new_zeros(crow.numel() - 1).index_add_(0, rows, (val != 0).to(x.dtype))
+    return spmm_csr(crow, col, val, x) / nnz.clamp_min(1.0).unsqueeze(1)
+
+
+def mean_weights(crow, val=None):
+    """Edge weights val / max(row count of nonzero val, 1) in float32 with IEEE
+    division: the exact values gnnc_mean_norm produces (val None: unit weights)."""
+    crow = torch.as_tensor(crow, dtype=torch.int64)
+    E = int(crow[-1])
+    val = torch.ones(E, dtype=torch.float32) if val is None else torch.as_tensor(val, dtype=torch.float32)
+    rows = torch.repeat_interleave(torch.arange(crow.numel() - 1), crow.diff())
+    nnz = torch.zeros(crow.numel() - 1, dtype=torch.int64).index_add_(0, rows, (val != 0).long())
+    return val / nnz.clamp_min(1).to(torch.float32)[rows]
+
+
+def sage_layer(x, crow, col, val, weight_l, bias_l, weight_r, act=None, log_softmax=False):
+    """PyG SAGEConv (mean, root weight) as the reference lowers it
+    (sage.raw.mlir:5-14): mean-aggregate x, linear with bias, plus a linear of x
+    without bias, then the activation."""
+    out = spmm_mean(crow, col, val, x) @ weight_l.t()
+    if bias_l is not None:
+        out = out + bias_l
+    out = out + x @ weight_r.t()
     out = _act(out, act)
     return F.log_softmax(out, dim=-1) if log_softmax else out
 
@@ -311,6 +346,19 @@ def gcn_forward(model, x, crow, col, val):
         h = gcn_layer(h, crow, col, val, conv.lin.weight.detach(),
                       None if conv.bias is None else conv.bias.detach(),
                       act=None if last else "relu", log_softmax=last)
+    return h
+
+
+def sage_forward(model, x, crow, col, val):
+    """Forward of the example SAGE model on a CSR adjacency, from its parameters."""
+    convs = [getattr(model, f"conv{i}") for i in range(1, model.num_layers + 1)]
+    h = x.to(torch.float32)
+    for i, conv in enumerate(convs):
+        last = i == len(convs) - 1
+        h = sage_layer(h, crow, col, val, conv.lin_l.weight.detach(),
+                       None if conv.lin_l.bias is None else conv.lin_l.bias.detach(),
+                       conv.lin_r.weight.detach(), act=None if last else "relu",
+                       log_softmax=last)
     return h
 
 

@@ -11,6 +11,8 @@ reference tree. Fixtures:
                     (4-byte alignment header, then little-endian float32).
   gat_toy.npz       lin / att_src / att_dst of GATConv(4, 2, heads=2) from
                     experiments/gatconv/dumps/gat.1-raw-torch.mlir:137-139.
+  sage_toy.npz      lin_l weight / bias and lin_r weight of the two SAGEConv layers of
+                    the SAGE toy model, from test/reference/sage.raw.mlir:35-40.
   kat_softmax.npz   the 64x32 output of the row-max / exp-sum / weighted-aggregate
                     probe, parsed from experiments/gat-gpu-codegen/dumps/cpu.out.txt.
   kat_spmm.npz      the 8x8 and 8x4 SpMM outputs of
@@ -70,6 +72,16 @@ def main(root: Path) -> None:
         att_src=g["torch_tensor_1_2_2_torch.float32"].reshape(1, 2, 2),
         att_dst=g["torch_tensor_1_2_2_torch.float32_1"].reshape(1, 2, 2),
         edge_index=np.array([[0, 1, 0], [1, 2, 2]], dtype=np.int64),
+    )
+    sg = _resources(root / "test/reference/sage.raw.mlir")
+    np.savez(
+        HERE / "sage_toy.npz",
+        wl1=sg["torch_tensor_8_4_torch.float32"].reshape(8, 4),
+        bl1=sg["torch_tensor_8_torch.float32"],
+        wr1=sg["torch_tensor_8_4_torch.float32_1"].reshape(8, 4),
+        wl2=sg["torch_tensor_3_8_torch.float32"].reshape(3, 8),
+        bl2=sg["torch_tensor_3_torch.float32"],
+        wr2=sg["torch_tensor_3_8_torch.float32_1"].reshape(3, 8),
     )
     np.savez(HERE / "kat_softmax.npz",
              y=_memref(root / "experiments/gat-gpu-codegen/dumps/cpu.out.txt"))

@@ -288,3 +288,55 @@ def test_softmax_aggregate_bf16_narrow(device):
     ref = O.softmax_aggregate(rowptr.cpu().long(), col.cpu().long(), s.double(), h_host.double(),
                               eps=1e-16)
     assert_close(out, ref)
+
+
+
+def test_mean_norm_is_bit_exact(device):
+    """gnnc_mean_norm: value / max(count of nonzero values in the row, 1), IEEE
+    division; zero values stay zero and do not count; empty rows are fine."""
+    from gnnc.b200 import runtime as rt
+
+    n = 3000
+    ei = random_graph(n, 40000, 17, heavy=((3, 5000),))
+    rowptr, col, _ = rt.csr_from_coo(ei.to(device), n, self_loops=False, dedupe=False)
+    g = torch.Generator().manual_seed(17)
+    val = torch.rand(col.numel(), generator=g)
+    val[torch.rand(col.numel(), generator=g) < 0.2] = 0.0
+    w = rt.mean_norm(rowptr, val.to(device)).cpu()
+    assert torch.equal(w, O.mean_weights(rowptr.cpu(), val))
+    w1 = rt.mean_norm(rowptr).cpu()
+    assert torch.equal(w1, O.mean_weights(rowptr.cpu()))
+
+
+@pytest.mark.parametrize(
+    "F,dtype,act,lsm,cta,split",
+    [(7, torch.float32, 1, False, 0, 0), (47, torch.bfloat16, 0, True, 0, 0),
+     (256, torch.bfloat16, 1, False, 0, 0), (256, torch.float32, 2, False, 16, 64),
+     (600, torch.float32, 1, False, 0, 0)],
+)
+def test_sage_aggregate_matches_oracle(device, F, dtype, act, lsm, cta, split):
+    """out = A_mean . h + root + bias (then act / log_softmax) over warp, CTA and
+    split rows, with the root term in both epilogues."""
+    from gnnc.b200 import runtime as rt
+
+    n = 2500
+    ei = random_graph(n, 30000, F, heavy=((5, 9000), (9, 300)))
+    rowptr, col, mult = rt.csr_from_coo(ei.to(device), n, self_loops=True, dedupe=True)
+    _, _, wn = rt.gcn_norm(rowptr, col, mult)
+    w = rt.mean_norm(rowptr, wn)
+    g = torch.Generator().manual_seed(F)
+    h_host = torch.randn(n, F, generator=g).to(dtype)
+    root_host = torch.randn(n, F, generator=g).to(dtype)
+    h = rt.empty_rows(n, F, dtype, device)
+    h.copy_(h_host)
+    root = rt.empty_rows(n, F, dtype, device)
+    root.copy_(root_host)
+    bias = torch.randn(F, generator=g)
+    out = rt.sage_aggregate(_plan(rowptr, cta, split), rowptr, col, w, h, root,
+                            bias=bias.to(device), act=act, log_softmax=lsm)
+    agg = O.spmm_csr(rowptr.cpu(), col.cpu(), w.cpu().double(), h_host.double())
+    ref = agg + root_host.double() + bias.double()
+    ref = {0: ref, 1: torch.relu(ref), 2: torch.nn.functional.elu(ref)}[act]
+    if lsm:
+        ref = torch.log_softmax(ref, dim=-1)
+    assert_close(out, ref)

@@ -13,7 +13,7 @@ from gnnc.pipeline.phase import PhaseNotReached, PhasePipeline
 
 
 def test_available_models():
-    assert available() == ["gat", "gcn"]
+    assert available() == ["gat", "gcn", "sage"]
 
 
 def test_phase_pipeline_stop_and_print():
@@ -38,17 +38,21 @@ def test_phase_pipeline_stop_and_print():
         p.add_callable_phase("a", lambda m: m)
 
 
-@pytest.mark.parametrize("model_name", ["gcn", "gat"])
+@pytest.mark.parametrize("model_name", ["gcn", "gat", "sage"])
 def test_lowering_fuses_epilogues(model_name):
     model, inputs = get_model_and_data(MODELS_DIR / f"{model_name}.py")
     prog, trace = lower(model, inputs, stop_after="b200-lower")
     assert [t[0] for t in trace] == ["import", "b200-lower"]
     assert [layer.kind for layer in prog.layers] == [model_name, model_name]
     first, last = prog.layers
-    assert first.act == (1 if model_name == "gcn" else 2)  # relu / elu
+    assert first.act == (2 if model_name == "gat" else 1)  # elu / relu
     assert last.log_softmax and not first.log_softmax
     if model_name == "gat":
         assert first.heads == 2 and first.concat and not last.concat
+    if model_name == "sage":
+        # lin_l with bias for the neighbour mean, lin_r for the root
+        assert first.weight_root is not None and first.bias is not None
+        assert tuple(first.weight.shape) == tuple(first.weight_root.shape) == (8, 4)
 
 
 def test_lowering_rejects_unsupported_ops():
@@ -79,6 +83,7 @@ def test_bench_cli_exit_codes(capsys):
 
     assert main(["--model", "gcn", "--target", "cpu"]) == 3
     assert main(["--model", "gat", "--dataset", "c1"]) == 2  # c1 is a GCN workload
+    assert main(["--model", "sage", "--dataset", "c2"]) == 2  # c2 is a GAT workload
 
 
 def test_synthetic_c1_exact_shape_and_deterministic():

@@ -193,3 +193,51 @@ def test_rows_fp64_matches_layer():
     adst = (h * a_d).sum(-1)
     got = O.gat_rows_fp64(rowptr, col, h.view(n, -1), asrc, adst, H, chunk_edges=37)
     np.testing.assert_allclose(got.numpy(), ref.double().numpy(), rtol=1e-5, atol=1e-6)
+
+
+def test_sage_toy_weights_replay_bit_exact():
+    """The SAGE toy model under seed 0 reproduces the weights embedded in
+    test/reference/sage.raw.mlir (PyG Linear's kaiming / uniform init, drawn
+    twice per Linear as PyG does)."""
+    from gnnc.examples.models import sage
+
+    fx = np.load(GOLDEN / "sage_toy.npz")
+    m = sage.Model(*sage.get_init_inputs())
+    for i in (1, 2):
+        conv = getattr(m, f"conv{i}")
+        assert np.array_equal(conv.lin_l.weight.detach().numpy(), fx[f"wl{i}"])
+        assert np.array_equal(conv.lin_l.bias.detach().numpy(), fx[f"bl{i}"])
+        assert np.array_equal(conv.lin_r.weight.detach().numpy(), fx[f"wr{i}"])
+
+
+def test_sage_toy_oracle_matches_dense_and_eager():
+    """sage.raw.mlir:5-27 restated densely in float64: mean over the row's nonzero
+    entries, lin_l with bias, plus lin_r, relu; layer 2; log_softmax."""
+    from gnnc.examples.models import sage
+
+    m = sage.Model(*sage.get_init_inputs())
+    x, adj = sage.get_inputs()
+    crow, col, val = adj.crow_indices(), adj.col_indices(), adj.values()
+    n = x.size(0)
+    a = torch.from_numpy(_dense_adj(crow.numpy(), col.numpy(), val.numpy(), n))
+    nnz = (a != 0).sum(1).clamp_min(1).double()
+    h = x.double()
+    for i in (1, 2):
+        conv = getattr(m, f"conv{i}")
+        wl, bl = conv.lin_l.weight.double(), conv.lin_l.bias.double()
+        wr = conv.lin_r.weight.double()
+        h = ((a @ h) / nnz[:, None]) @ wl.t() + bl + h @ wr.t()
+        h = torch.relu(h) if i == 1 else torch.log_softmax(h, dim=-1)
+    ref = O.sage_forward(m, x, crow, col, val)
+    np.testing.assert_allclose(ref.double().numpy(), h.detach().numpy(), rtol=1e-6, atol=1e-6)
+    with torch.no_grad():
+        eager = m(x, adj)
+    np.testing.assert_allclose(eager.numpy(), ref.numpy(), rtol=1e-6, atol=1e-6)
+
+
+def test_mean_weights_count_nonzero_values():
+    crow = torch.tensor([0, 3, 3, 5])
+    val = torch.tensor([0.5, 0.0, 2.0, 1.0, 3.0])
+    w = O.mean_weights(crow, val)
+    assert torch.equal(w, torch.tensor([0.25, 0.0, 1.0, 0.5, 1.5]))
+    assert torch.equal(O.mean_weights(crow), torch.tensor([1 / 3, 1 / 3, 1 / 3, 0.5, 0.5]))
