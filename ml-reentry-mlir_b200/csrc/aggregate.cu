@@ -783,9 +783,15 @@ __global__ void __launch_bounds__(kThreads, 4) agg_kernel(const AggParams p) {
     t = __shfl_sync(kFull, t, 0);
     if (t >= p.n_warp_tasks) break;
     const int r0 = p.warp_tasks[t], r1 = p.warp_tasks[t + 1];
-    for (int r = r0; r < r1; ++r) {
-      const int eb = max(int64_t(__ldg(p.rowptr + r)), p.e_lo);
-      const int ee = min(int64_t(__ldg(p.rowptr + r + 1)), p.e_hi);
+    // The task's row pointers come in with one load per 31 rows (lane i holds
+    // rowptr[rb + i]) instead of two dependent loads at the head of each row.
+    for (int rb = r0; rb < r1; rb += 31) {
+    const int nr = min(31, r1 - rb);
+    const int rpv = lane <= nr ? __ldg(p.rowptr + rb + lane) : 0;
+    for (int i = 0; i < nr; ++i) {
+      const int r = rb + i;
+      const int eb = max(int64_t(__shfl_sync(kFull, rpv, i)), p.e_lo);
+      const int ee = min(int64_t(__shfl_sync(kFull, rpv, i + 1)), p.e_hi);
       if (ee - eb > p.cta_threshold) continue;
       float acc[NV][VEC], s_acc[NV], inv[NV];
 #pragma unroll
@@ -810,6 +816,7 @@ __global__ void __launch_bounds__(kThreads, 4) agg_kernel(const AggParams p) {
         warp_epilogue(p, r, s_row, lane);
         __syncwarp();
       }
+    }
     }
   }
 }
