@@ -653,6 +653,162 @@ struct AggNarrow {
   }
 };
 
+// Phase 2 of agg_kernel for narrow bf16 rows (32 < F <= 64) with one head or
+// GCN weights (written for up to four heads): one destination row per 8-lane group,
+// four rows per warp at a time, so four rows' chains of dependent loads (col,
+// then a_src, then h) overlap instead of running one after another. Within a
+// group, lane l scores edge 8c + l of chunk c (group-wide max by xor
+// shuffles, online softmax across chunks), then every lane gathers its 16-byte
+// slice of the chunk's h rows in edge order and folds it in, as the one-row
+// loops do. The warp runs as many chunks as its longest row needs; finished
+// groups idle through the rest. Rows above the CTA threshold are skipped.
+template <int KH>
+__device__ __forceinline__ void narrow_rows(const AggParams& p, int32_t* s_col, float* s_p,
+                                            int lane, bool softmax) {
+  constexpr int HS = KH == 0 ? 1 : (KH | 1);
+  constexpr int KX = KH > 0 ? KH : 1;
+  const int lig = lane & 7, grp = lane >> 3;
+  const bool vok = lig * 8 < p.F;
+  const char* hlane = reinterpret_cast<const char*>(p.h) + lig * 16;
+  const uint32_t ldh_b = uint32_t(p.ldh) * 2u;
+  const int hv = KH > 1 ? min((lig * 8) / p.C, KH - 1) : 0;
+  const float* s_pg = s_p + (grp * 8) * HS + hv;
+  const int32_t* s_cg = s_col + grp * 8;
+  for (;;) {
+    int t = 0;
+    if (lane == 0) t = atomicAdd(p.counters + 1, 1);
+    t = __shfl_sync(kFull, t, 0);
+    if (t >= p.n_warp_tasks) break;
+    const int r0 = p.warp_tasks[t], r1 = p.warp_tasks[t + 1];
+    for (int rb = r0; rb < r1; rb += 4) {
+      const int r = rb + grp;
+      int eb = 0, ee = 0;
+      bool active = r < r1;
+      if (active) {
+        eb = int(max(int64_t(__ldg(p.rowptr + r)), p.e_lo));
+        ee = int(min(int64_t(__ldg(p.rowptr + r + 1)), p.e_hi));
+        if (ee - eb > p.cta_threshold) active = false;
+      }
+      if (!active) eb = ee = 0;
+      float ad[KX], m[KX];
+#pragma unroll
+      for (int hd = 0; hd < KX; ++hd) {
+        ad[hd] = (KH > 0 && active && p.mode == MODE_GAT) ? __ldg(p.adst + size_t(r) * KH + hd)
+                                                           : 0.f;
+        m[hd] = -INFINITY;
+      }
+      float acc[8], s_acc = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+      const int nch = __reduce_max_sync(kFull, unsigned(ee - eb + 7) >> 3);
+      for (int c = 0; c < int(nch); ++c) {
+        const int k = eb + c * 8 + lig;
+        bool valid = k < ee;
+        int src = valid ? __ldg(p.col + k) : 0;
+        if (valid && unsigned(src) >= unsigned(p.n_src)) {
+          atomicOr(p.counters + 2, 1);
+          valid = false;
+          src = 0;
+        }
+        s_col[lane] = src;
+        if constexpr (KH == 0) {
+          s_p[lane] = valid ? __ldg(p.w + k) : 0.f;
+        } else {
+          const float* xs = p.mode == MODE_GAT ? p.asrc + size_t(src) * KH
+                                               : p.scores + size_t(valid ? k : 0) * KH;
+          bool rescale = false;
+          float scl = 1.f;
+#pragma unroll
+          for (int hd = 0; hd < KH; ++hd) {
+            float e = -INFINITY;
+            if (valid) {
+              const float x = __ldg(xs + hd);
+              if (p.mode == MODE_GAT) {
+                const float tt = x + ad[hd];
+                e = tt > 0.f ? tt : tt * p.slope;
+              } else {
+                e = x;
+              }
+            }
+            float cmax = e;  // group-wide max: the xor partners stay inside the 8-lane group
+            cmax = fmaxf(cmax, __shfl_xor_sync(kFull, cmax, 4));
+            cmax = fmaxf(cmax, __shfl_xor_sync(kFull, cmax, 2));
+            cmax = fmaxf(cmax, __shfl_xor_sync(kFull, cmax, 1));
+            const float m_new = fmaxf(m[hd], cmax);
+            const float pr = valid ? __expf(e - m_new) : 0.f;
+            if (hd == hv) {
+              rescale = (c > 0) && (m_new != m[hd]);
+              scl = __expf(m[hd] - m_new);
+            }
+            m[hd] = m_new;
+            s_p[lane * HS + hd] = pr;
+          }
+          if (rescale) {  // uniform within the group; no shuffle below
+            s_acc *= scl;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] *= scl;
+          }
+        }
+        __syncwarp();
+        const int n = min(8, max(0, ee - (eb + c * 8)));
+        uint4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          v[u] = make_uint4(0u, 0u, 0u, 0u);
+          if (vok && u < n)
+            v[u] = __ldg(reinterpret_cast<const uint4*>(hlane + size_t(uint32_t(s_cg[u])) * ldh_b));
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (u < n) {
+            const float a = s_pg[u * HS];
+            s_acc += a;
+            AggFast<KH>::fma_row(acc, a, v[u]);
+          }
+        }
+        __syncwarp();
+      }
+      // Epilogue of the group's row: lane lig holds features [8 lig, 8 lig + 8).
+      const float inv = (softmax && ee > eb) ? 1.f / (s_acc + p.eps) : 1.f;
+      const int e0 = lig * 8;
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const bool ok = active && e0 + e < p.F;
+        float v = acc[e] * inv;
+        if (ok && p.root) v += load_val(p.root, p.root_dtype, size_t(r) * size_t(p.ldr) + e0 + e);
+        if (ok && p.bias) v += __ldg(p.bias + e0 + e);
+        o[e] = apply_act(v, p.act);
+      }
+      if (p.log_softmax) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e0 + e < p.F) mx = fmaxf(mx, o[e]);
+        mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 2));
+        mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 1));
+        float se = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e0 + e < p.F) se += expf(o[e] - mx);
+        se += __shfl_xor_sync(kFull, se, 4);
+        se += __shfl_xor_sync(kFull, se, 2);
+        se += __shfl_xor_sync(kFull, se, 1);
+        const float lse = logf(se);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = (o[e] - mx) - lse;
+      }
+      if (active) {
+        const size_t base = size_t(r) * size_t(p.ldo) + e0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e0 + e < p.F) store_val(p.out, p.out_dtype, base + e, o[e]);
+      }
+    }
+  }
+}
+
 // Selects the edge loop: the specialised one for KH >= 0, the generic otherwise.
 template <typename TH, int VEC, int LPG, int NV, int KH>
 struct EdgeLoop {
@@ -777,6 +933,14 @@ __global__ void __launch_bounds__(kThreads, 4) agg_kernel(const AggParams p) {
   }
 
   // ---- Phase 2: one warp per short row, edge-balanced row ranges ----
+  // (one head or GCN weights: measured faster than the one-row loop; with
+  // four heads the per-head group reductions cost more than the overlap gains)
+  if constexpr (KH >= 0 && KH <= 1 && LPG == 8 && NV == 1 && VEC == 8) {
+    if (p.concat || p.H == 1) {
+      narrow_rows<KH>(p, s_col, s_p, lane, softmax);
+      return;
+    }
+  }
   for (;;) {
     int t = 0;
     if (lane == 0) t = atomicAdd(p.counters + 1, 1);
