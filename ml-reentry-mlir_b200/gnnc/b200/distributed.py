@@ -1,0 +1,312 @@
+"""Whole-model forward on `world` GPUs, one process per GPU.
+
+The reference has no multi-GPU path (internal-docs/project-summary.md:105).
+Here a lowered model (B200Executable) runs its layers partitioned by
+destination row: rank r owns rows [r*R, (r+1)*R), R = ceil(N / world), their
+input features and their output rows. Each layer has one exchange step, over
+the narrower side of its projection:
+
+* input exchange (the layer's input is narrower than its projected rows, e.g.
+  100 -> 4 x 64): every rank keeps its input rows in its slot of a
+  [world*R, K] table; the copy engines pull the other slots from the owners'
+  HBM (CUDA IPC mapping, gnnc_peer_copy) piece by piece while the projection
+  runs on the pieces already present, so every rank projects all rows;
+* output exchange (the projected rows are narrower, e.g. 256 -> 47): each rank
+  projects its own rows into its slot of the [world*R, F] table (and a_src's
+  for GAT), and the other slots are pulled the same way.
+
+The layer's aggregation then reads local memory only and writes its rows
+straight into the next layer's input slot. A fence orders each exchanged
+buffer's writes before the peers' reads (a one-word NCCL all-reduce on the
+stream, or a host barrier for gloo process groups), and one more at the end of
+the forward orders the last reads before the next forward's writes. The
+results are those of the single-GPU executable, row for row: every row is
+projected and aggregated by the same kernels on the same values.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from gnnc.b200 import partition as P
+from gnnc.b200 import runtime as rt
+from gnnc.b200.program import B200Executable
+
+
+@dataclass
+class _Layer:
+    mode: str  # "input" | "output"
+    rowptr: torch.Tensor
+    col: torch.Tensor
+    w: torch.Tensor | None
+    plan: rt.Plan
+    table: torch.Tensor  # exchanged [world*R, ld] (input rows or projected rows)
+    peers: _PeerTable
+    in_own: torch.Tensor  # this rank's input rows [R, ld_in] (a view of table for input mode)
+    h_full: torch.Tensor  # projected rows of every node [world*R, F]
+    a_full: torch.Tensor | None  # GAT a_src [world*R, H] (exchanged in output mode)
+    a_peers: _PeerTable | None
+    d_full: torch.Tensor | None  # GAT a_dst [world*R, H] (own rows used)
+    root: torch.Tensor | None  # SAGE lin_r rows of this rank [R, F]
+
+
+class _PeerTable:
+    """Every rank's copy of one [world*R, ld] table, mapped into this process;
+    slot(p, a, b) addresses rows [a, b) of rank p's own slot in rank p's table."""
+
+    def __init__(self, table: torch.Tensor, rr: P.RowRange, group) -> None:
+        import torch.distributed as dist
+
+        self.table, self.rr = table, rr
+        meta: list = [None] * rr.world
+        dist.all_gather_object(meta, rt.peer_export(table), group=group)
+        self.ptrs: list[int] = []
+        self._opened: list[tuple[int, int]] = []
+        for p in range(rr.world):
+            if p == rr.rank:
+                self.ptrs.append(table.data_ptr())
+            else:
+                handle, off = meta[p]
+                ptr = rt.peer_open(table.device, handle, off)
+                self._opened.append((ptr, off))
+                self.ptrs.append(ptr)
+
+    def slot(self, p: int, a: int, b: int) -> rt.DeviceRows:
+        t = self.table
+        row_bytes = t.stride(0) * t.element_size()
+        base = self.ptrs[p] + (p * self.rr.rows_per_rank + a) * row_bytes
+        return rt.DeviceRows(base, b - a, t.size(1), t.stride(0), t.dtype, t.device)
+
+    def close(self) -> None:
+        for ptr, off in self._opened:
+            rt.peer_close(self.table.device, ptr, off)
+        self._opened = []
+
+
+class DistributedExecutable:
+    """A B200Executable run partitioned over the ranks of `group`.
+
+    Call with (x_rows, graph): x_rows are this rank's input rows
+    [rows of row_range(N, world, rank)], graph the whole graph (the adjacency
+    or edge_index every rank holds). Returns this rank's output rows."""
+
+    PIECE_ROWS = 1 << 18
+
+    def __init__(self, exe: B200Executable, group=None, fence: str = "auto") -> None:
+        import torch.distributed as dist
+
+        self.exe, self.program, self.device = exe, exe.program, exe.device
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if fence == "auto":
+            fence = "nccl" if dist.get_backend(group) == "nccl" else "host"
+        if fence not in ("nccl", "host"):
+            raise ValueError(f"unknown fence {fence!r}")
+        self.fence_kind = fence
+        self._fence_buf = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._side = torch.cuda.Stream(self.device)
+        self._key = None
+        self._layers: list[_Layer] = []
+        self._out: torch.Tensor | None = None
+        self._rr: P.RowRange | None = None
+
+    # -- set-up ------------------------------------------------------------
+
+    def _fence(self) -> None:
+        import torch.distributed as dist
+
+        if self.fence_kind == "nccl":
+            dist.all_reduce(self._fence_buf, group=self.group)
+        else:
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+
+    def exchange_modes(self) -> list[str]:
+        """Per layer, the side of the projection that crosses NVLink."""
+        s = torch.empty((), dtype=self.program.feature_dtype).element_size()
+        modes = []
+        for layer in self.program.layers:
+            in_b = rt.row_stride(layer.in_channels, self.program.feature_dtype) * s
+            out_b = rt.row_stride(layer.width, self.program.feature_dtype) * s
+            if layer.kind == "gat":
+                out_b += 4 * layer.heads
+            modes.append("input" if in_b <= out_b else "output")
+        return modes
+
+    def _setup(self, x_rows: torch.Tensor, graph: torch.Tensor) -> None:
+        import torch.distributed as dist
+
+        counts: list = [None] * self.world
+        dist.all_gather_object(counts, int(x_rows.size(0)), group=self.group)
+        N = int(sum(counts))
+        rr = P.row_range(N, self.world, self.rank)
+        if [P.row_range(N, self.world, r).count for r in range(self.world)] != counts:
+            raise ValueError(f"ranks hold {counts} rows; row_range({N}, {self.world}) expects "
+                             "equal contiguous ranges")
+        self.close()
+        self._rr, R, W = rr, rr.rows_per_rank, self.world
+        self._key = (None, N)
+        dev, dt = self.device, self.program.feature_dtype
+        layers = []
+        modes = self.exchange_modes()
+        for layer, mode in zip(self.program.layers, modes, strict=True):
+            g = self.exe._graph_for(graph, N, layer)
+            extra = () if g.w is None else (g.w,)
+            parts = P.local_csr(g.rowptr, g.col, rr, extra)
+            rowptr_l, col_l = parts[0], parts[1]
+            w_l = parts[2] if g.w is not None else None
+            plan = rt.Plan(rowptr_l)
+            ld_in = rt.row_stride(layer.in_channels, dt)
+            ld_f = rt.row_stride(layer.width, dt)
+            gat = layer.kind == "gat"
+            H = layer.heads
+            h_full = torch.zeros((W * R, ld_f), dtype=dt, device=dev)
+            a_full = torch.zeros((W * R, H), dtype=torch.float32, device=dev) if gat else None
+            d_full = torch.zeros((W * R, H), dtype=torch.float32, device=dev) if gat else None
+            if mode == "input":
+                table = torch.zeros((W * R, ld_in), dtype=dt, device=dev)
+                in_own = table[rr.begin : rr.begin + R]
+                peers, a_peers = _PeerTable(table, rr, self.group), None
+            else:
+                table = h_full
+                in_own = torch.zeros((R, ld_in), dtype=dt, device=dev)
+                peers = _PeerTable(table, rr, self.group)
+                a_peers = _PeerTable(a_full, rr, self.group) if gat else None
+            root = (torch.zeros((R, ld_f), dtype=dt, device=dev)
+                    if layer.kind == "sage" else None)
+            layers.append(_Layer(mode, rowptr_l, col_l, w_l, plan, table, peers, in_own, h_full,
+                                 a_full, a_peers, d_full, root))
+        last = self.program.layers[-1]
+        self._out = rt.empty_rows(R, last.out_width, self.program.output_dtype, dev)
+        self._layers = layers
+        self._key = (self.exe._graph_key(graph), N)
+
+    def close(self) -> None:
+        """Unmaps the peers' tables (collective: every rank calls it)."""
+        for L in self._layers:
+            L.peers.close()
+            if L.a_peers is not None:
+                L.a_peers.close()
+        self._layers = []
+        self._key = None
+
+    # -- forward -----------------------------------------------------------
+
+    def _pull(self, table: _PeerTable, dst: torch.Tensor, events: list) -> None:
+        """Copies every other rank's slot of `table` into the same rows of
+        `dst`, in pieces on the side stream; appends (row slice, event) per
+        piece to `events`. Owners are read in rotated order (rank r reads r+1,
+        r+2, ...), so at any time each owner serves one reader."""
+        rr, R, N = self._rr, self._rr.rows_per_rank, self._key[1]
+        row_bytes = dst.stride(0) * dst.element_size()
+        for k in range(1, self.world):
+            p = (rr.rank + k) % self.world
+            n_p = P.row_range(N, rr.world, p).count
+            for a in range(0, n_p, self.PIECE_ROWS):
+                b = min(n_p, a + self.PIECE_ROWS)
+                rt.peer_copy(dst[p * R + a :], table.slot(p, a, b), (b - a) * row_bytes)
+                ev = torch.cuda.Event()
+                ev.record(self._side)
+                events.append((slice(p * R + a, p * R + b), ev))
+
+    def run_device(self, x_rows: torch.Tensor, graph: torch.Tensor) -> torch.Tensor:
+        """Forward of this rank's rows; returns them on the device. Collective:
+        every rank of the group calls it with the same graph."""
+        if self._key is None or self._key[0] != self.exe._graph_key(graph):
+            self._setup(x_rows, graph)
+        rr = self._rr
+        n, dt = rr.count, self.program.feature_dtype
+        cur = torch.cuda.current_stream(self.device)
+        layers = self.program.layers
+        with torch.cuda.device(self.device):
+            first = self._layers[0]
+            first.in_own[:n, : layers[0].in_channels].copy_(x_rows, non_blocking=True)
+            for i, (layer, L, (w, asw, adw, bias), wr) in enumerate(
+                zip(layers, self._layers, self.exe._weights, self.exe._roots, strict=True)
+            ):
+                last = i == len(layers) - 1
+                K, F = layer.in_channels, layer.width
+                gat = layer.kind == "gat"
+
+                def proj(x, rows: slice):
+                    if gat:
+                        rt.proj(x, w, att_src=asw, att_dst=adw, heads=layer.heads, out_dtype=dt,
+                                out=L.h_full[rows, :F], asrc_out=L.a_full[rows],
+                                adst_out=L.d_full[rows])
+                    else:
+                        rt.proj(x, w, out_dtype=dt, out=L.h_full[rows, :F])
+
+                own = slice(rr.begin, rr.begin + n)
+                events: list = []
+                if L.mode == "input":
+                    self._fence()  # this layer's input rows are written on every rank
+                    self._side.wait_stream(cur)
+                    with torch.cuda.stream(self._side):
+                        self._pull(L.peers, L.table, events)
+                    if n:
+                        proj(L.in_own[:n, :K], own)
+                    for rows, ev in events:
+                        cur.wait_event(ev)
+                        proj(L.table[rows, :K], rows)
+                else:
+                    if n:
+                        proj(L.in_own[:n, :K], own)
+                    self._fence()  # projected rows written everywhere
+                    self._side.wait_stream(cur)
+                    with torch.cuda.stream(self._side):
+                        self._pull(L.peers, L.h_full, events)
+                        if gat:
+                            self._pull(L.a_peers, L.a_full, events)
+                    for _, ev in events:
+                        cur.wait_event(ev)
+                if layer.kind == "sage" and n:
+                    rt.proj(L.in_own[:n, :K], wr, out_dtype=dt, out=L.root[:n, :F])
+                if last:
+                    out = self._out[:n]
+                else:
+                    nxt = self._layers[i + 1]
+                    out = nxt.in_own[:n, : layers[i + 1].in_channels]
+                if n:
+                    self._aggregate(layer, L, n, bias, out)
+            self._fence()  # every peer is done reading this forward's rows
+        return self._out[:n]
+
+    def _aggregate(self, layer, L: _Layer, n: int, bias, out: torch.Tensor) -> None:
+        N, F = self._key[1], layer.width
+        rr = self._rr
+        h = L.h_full[:N, :F]
+        if layer.kind == "gat":
+            rt.gat_aggregate(L.plan, L.rowptr, L.col, h, L.a_full[:N],
+                             L.d_full[rr.begin : rr.begin + n], heads=layer.heads,
+                             negative_slope=layer.negative_slope, concat=layer.concat,
+                             bias=bias, act=layer.act, log_softmax=layer.log_softmax,
+                             out_dtype=out.dtype, out=out)
+        elif layer.kind == "sage":
+            rt.sage_aggregate(L.plan, L.rowptr, L.col, L.w, h, L.root[:n, :F], bias=bias,
+                              act=layer.act, log_softmax=layer.log_softmax, out_dtype=out.dtype,
+                              out=out)
+        else:
+            rt.gcn_aggregate(L.plan, L.rowptr, L.col, L.w, h, bias=bias, act=layer.act,
+                             log_softmax=layer.log_softmax, out_dtype=out.dtype, out=out)
+
+    def __call__(self, x_rows: torch.Tensor, graph: torch.Tensor) -> torch.Tensor:
+        out = self.run_device(x_rows, graph)
+        if not x_rows.is_cuda:
+            host = torch.empty(tuple(out.shape), dtype=out.dtype, pin_memory=True)
+            host.copy_(out, non_blocking=True)
+            torch.cuda.current_stream(self.device).synchronize()
+            return host
+        return out.contiguous()
+
+
+def distribute(exe: B200Executable, group=None, fence: str = "auto") -> DistributedExecutable:
+    """Wraps a compiled executable for a row-partitioned forward over `group`."""
+    if not isinstance(exe, B200Executable):
+        raise NotImplementedError(f"cannot distribute {type(exe).__name__}")
+    return DistributedExecutable(exe, group=group, fence=fence)
+
+
+__all__ = ["DistributedExecutable", "distribute"]
