@@ -69,14 +69,22 @@ def _dataset_inputs(model_name: str, dataset: str):
 
     if dataset not in ("cora", "ogbn-arxiv"):
         return synthetic_inputs(model_name, dataset)
-    if dataset == "cora":
-        from torch_geometric.datasets import Planetoid
+    try:  # the reference's loaders, when PyG / OGB are installed
+        if dataset == "cora":
+            from torch_geometric.datasets import Planetoid
 
-        ds = Planetoid(root=str(DATA_DIR / "planetoid"), name="Cora")
-    else:
-        from ogb.nodeproppred import PygNodePropPredDataset
+            ds = Planetoid(root=str(DATA_DIR / "planetoid"), name="Cora")
+        else:
+            from ogb.nodeproppred import PygNodePropPredDataset
 
-        ds = PygNodePropPredDataset(name="ogbn-arxiv", root=str(DATA_DIR / "ogb"))
+            ds = PygNodePropPredDataset(name="ogbn-arxiv", root=str(DATA_DIR / "ogb"))
+    except ImportError:  # the same raw files, read without them
+        from gnnc.datasets import load
+
+        x, edge_index, _, num_classes = load(dataset, DATA_DIR)
+        graph = (normalized_csr_adj(edge_index, x.size(0)) if model_name in ("gcn", "sage")
+                 else edge_index)
+        return (x, graph), (x.size(1), _DEFAULT_HIDDEN, num_classes), {}
     data = ds[0]
     graph = (normalized_csr_adj(data.edge_index, data.num_nodes) if model_name in ("gcn", "sage")
              else data.edge_index)
