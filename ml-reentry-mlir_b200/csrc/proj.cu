@@ -128,6 +128,67 @@ __global__ void __launch_bounds__(kThreads) proj_simt_kernel(const ProjParams p)
   }
 }
 
+// fp32 operands on the tensor cores. Each value splits into three bf16 parts,
+// v0 = bf16(v), v1 = bf16(v - v0), v2 = bf16(v - v0 - v1) (24 significant
+// bits together), and x.w = x0.w0 + x0.w1 + x1.w0 + x0.w2 + x1.w1 + x2.w0 up
+// to the dropped cross terms, which are below 2^-24 of |x||w|: one bf16 GEMM
+// with fp32 accumulation over the six K-blocks [x0 x0 x1 x0 x1 x2] against
+// [w0 w1 w0 w2 w1 w0]. This kernel writes the six blocks of one operand
+// (pattern 0: x's, pattern 1: w's) for `rows` rows into out (row stride ldo).
+__global__ void split3_kernel(const float* __restrict__ in, int64_t ldi, int64_t rows, int64_t K,
+                              __nv_bfloat16* __restrict__ out, int64_t ldo, int pattern) {
+  const int px[6] = {0, 0, 1, 0, 1, 2};
+  const int pw[6] = {0, 1, 0, 2, 1, 0};
+  const int64_t total = rows * K;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = i / K, k = i - r * K;
+    const float v = in[r * ldi + k];
+    __nv_bfloat16 part[3];
+    part[0] = __float2bfloat16_rn(v);
+    const float r1 = v - __bfloat162float(part[0]);
+    part[1] = __float2bfloat16_rn(r1);
+    part[2] = __float2bfloat16_rn(r1 - __bfloat162float(part[1]));
+    __nv_bfloat16* o = out + r * ldo + k;
+#pragma unroll
+    for (int s = 0; s < 6; ++s) o[s * K] = part[pattern ? pw[s] : px[s]];
+  }
+}
+
+// fp32 x and w through the tcgen05 kernel as a bf16 GEMM over 6K (see
+// split3_kernel); kProjTcDeclined when the shapes or sizes do not suit it.
+int proj_f32_split3(gnnc_ctx_t* ctx, const float* x, int64_t ldx, const float* w, int64_t ldw,
+                    int64_t N, int64_t K, int64_t F, const float* att_src, const float* att_dst,
+                    int64_t H, void* h, int h_dtype, int64_t ldh, float* asrc, float* adst) {
+  // Worth it once the GEMM has some size; F beyond 256 is not a tcgen05 shape here.
+  if (F > 256 || N < 1024 || double(N) * double(K) * double(F) < double(1 << 24))
+    return gnnc::kProjTcDeclined;
+  // shapes the tcgen05 kernel declines: decide before splitting
+  const int hes = h_dtype == GNNC_BF16 ? 2 : 4;
+  if (att_src && !(H == 1 || (F / H) % 16 == 0)) return gnnc::kProjTcDeclined;
+  if (reinterpret_cast<uintptr_t>(h) % 16 || (ldh * hes) % 16 || F * hes < 16)
+    return gnnc::kProjTcDeclined;
+  const int64_t K6 = 6 * K;
+  const int64_t ld6 = (K6 + 7) / 8 * 8;
+  const size_t xb = size_t(N) * size_t(ld6) * 2, wb = size_t(F) * size_t(ld6) * 2;
+  if (!ctx->ws_owned && ctx->ws_bytes < xb + wb) return gnnc::kProjTcDeclined;  // bound, too small
+  int st = gnnc::ensure_workspace(ctx, xb + wb);
+  if (st) return st;
+  auto* x6 = reinterpret_cast<__nv_bfloat16*>(ctx->ws);
+  auto* w6 = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(ctx->ws) + xb);
+  const int threads = 256;
+  auto grid_of = [&](int64_t n) {
+    const int64_t g = (n + threads - 1) / threads;
+    const int64_t cap = int64_t(ctx->num_sms) * 16;
+    return unsigned(g < cap ? g : cap);
+  };
+  split3_kernel<<<grid_of(N * K), threads, 0, ctx->stream>>>(x, ldx, N, K, x6, ld6, 0);
+  split3_kernel<<<grid_of(F * K), threads, 0, ctx->stream>>>(w, ldw, F, K, w6, ld6, 1);
+  GNNC_CUDA_TRY(ctx, cudaGetLastError());
+  return gnnc::proj_tc_try(ctx, x6, ld6, w6, ld6, N, K6, F, att_src, att_dst, H, h, h_dtype, ldh,
+                           asrc, adst);
+}
+
 }  // namespace
 
 extern "C" int gnnc_proj(gnnc_ctx_t* ctx, const void* x, int x_dtype, int64_t ldx,
@@ -155,6 +216,12 @@ extern "C" int gnnc_proj(gnnc_ctx_t* ctx, const void* x, int x_dtype, int64_t ld
     int st = gnnc::proj_tc_try(ctx, x, ldx, w, ldw, N, K, F, att ? att_src : nullptr,
                                att ? att_dst : nullptr, att ? H : 1, h, h_dtype, ldh,
                                att ? asrc : nullptr, att ? adst : nullptr);
+    if (st != gnnc::kProjTcDeclined) return st;
+  } else {
+    int st = proj_f32_split3(ctx, static_cast<const float*>(x), ldx,
+                             static_cast<const float*>(w), ldw, N, K, F, att ? att_src : nullptr,
+                             att ? att_dst : nullptr, att ? H : 1, h, h_dtype, ldh,
+                             att ? asrc : nullptr, att ? adst : nullptr);
     if (st != gnnc::kProjTcDeclined) return st;
   }
   ProjParams p{};
