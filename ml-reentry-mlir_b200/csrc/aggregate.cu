@@ -809,6 +809,119 @@ __device__ __forceinline__ void narrow_rows(const AggParams& p, int32_t* s_col, 
   }
 }
 
+// Edge loop specialised for fp32 rows of 256 features (two 16-byte loads per
+// lane per edge, the Agg<float, 4, 32, 2> layout: lane l holds features
+// [4l, 4l+4) and [128+4l, 128+4l+4)) and a compile-time head count KH (0: GCN
+// weights): the AggFast scheme (unrolled heads, groups of four edges with
+// eight loads in flight, constant shared-memory offsets) with the same
+// arithmetic and order as Agg<float, 4, 32, 2>::range.
+template <int KH>
+struct AggFast32 {
+  static constexpr int HS = KH == 0 ? 1 : (KH | 1);
+
+  static __device__ __forceinline__ void fma4(float (&acc)[4], float a, const float4& v) {
+    ffma2(acc[0], acc[1], a, v.x, v.y);
+    ffma2(acc[2], acc[3], a, v.z, v.w);
+  }
+
+  static __device__ __forceinline__ void range(const AggParams& p, int64_t row, int eb, int ee,
+                                               float (&acc)[2][4], float (&s_acc)[2],
+                                               float& m_reg, int32_t* s_col, float* s_p,
+                                               const int (&hv)[2], int lane) {
+    const char* hl0 = reinterpret_cast<const char*>(p.h) + lane * 16;
+    const char* hl1 = hl0 + 512;
+    const size_t ldh_b = size_t(p.ldh) * 4u;
+    const float* s_ph0 = s_p + hv[0];
+    const float* s_ph1 = s_p + hv[1];
+    float sc_reg = 1.f;
+    float ad_reg = 0.f;
+    if (KH > 0 && p.mode == MODE_GAT && lane < KH) ad_reg = __ldg(p.adst + size_t(row) * KH + lane);
+    for (int cb = eb; cb < ee; cb += 32) {
+      const int k = cb + lane;
+      bool valid = k < ee;
+      int src = valid ? __ldg(p.col + k) : 0;
+      if (valid && unsigned(src) >= unsigned(p.n_src)) {
+        atomicOr(p.counters + 2, 1);
+        valid = false;
+        src = 0;
+      }
+      s_col[lane] = src;
+      if constexpr (KH == 0) {
+        s_p[lane] = valid ? __ldg(p.w + k) : 0.f;
+      } else {
+        const float* xs = p.mode == MODE_GAT ? p.asrc + size_t(src) * KH
+                                             : p.scores + size_t(valid ? k : cb) * KH;
+        bool rescale = false;
+#pragma unroll
+        for (int hd = 0; hd < KH; ++hd) {
+          const float ad = __shfl_sync(kFull, ad_reg, hd);  // every lane: outside `valid`
+          float e = -INFINITY;
+          if (valid) {
+            const float x = __ldg(xs + hd);
+            if (p.mode == MODE_GAT) {
+              const float t = x + ad;
+              e = t > 0.f ? t : t * p.slope;
+            } else {
+              e = x;
+            }
+          }
+          const float cmax = warp_max_redux(e);
+          const float m_old = __shfl_sync(kFull, m_reg, hd);
+          const float m_new = fmaxf(m_old, cmax);
+          const float pr = valid ? __expf(e - m_new) : 0.f;
+          const float sc = __expf(m_old - m_new);
+          if (lane == hd) {
+            sc_reg = sc;
+            m_reg = m_new;
+          }
+          rescale |= (cb != eb) && (m_new != m_old);
+          s_p[lane * HS + hd] = pr;
+        }
+        if (rescale) {  // warp-uniform
+#pragma unroll
+          for (int v = 0; v < 2; ++v) {
+            const float sc = __shfl_sync(kFull, sc_reg, hv[v]);
+            s_acc[v] *= sc;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[v][e] *= sc;
+          }
+        }
+      }
+      __syncwarp();
+      const int n = min(32, ee - cb);
+      int j = 0;
+      for (; j + 4 <= n; j += 4) {
+        float4 v0[4], v1[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const size_t off = size_t(uint32_t(s_col[j + u])) * ldh_b;
+          v0[u] = __ldg(reinterpret_cast<const float4*>(hl0 + off));
+          v1[u] = __ldg(reinterpret_cast<const float4*>(hl1 + off));
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float a0 = s_ph0[(j + u) * HS], a1 = s_ph1[(j + u) * HS];
+          s_acc[0] += a0;
+          fma4(acc[0], a0, v0[u]);
+          s_acc[1] += a1;
+          fma4(acc[1], a1, v1[u]);
+        }
+      }
+      for (; j < n; ++j) {
+        const size_t off = size_t(uint32_t(s_col[j])) * ldh_b;
+        const float4 v0 = __ldg(reinterpret_cast<const float4*>(hl0 + off));
+        const float4 v1 = __ldg(reinterpret_cast<const float4*>(hl1 + off));
+        const float a0 = s_ph0[j * HS], a1 = s_ph1[j * HS];
+        s_acc[0] += a0;
+        fma4(acc[0], a0, v0);
+        s_acc[1] += a1;
+        fma4(acc[1], a1, v1);
+      }
+      __syncwarp();
+    }
+  }
+};
+
 // Selects the edge loop: the specialised one for KH >= 0, the generic otherwise.
 template <typename TH, int VEC, int LPG, int NV, int KH>
 struct EdgeLoop {
@@ -821,6 +934,14 @@ struct EdgeLoop<__nv_bfloat16, 8, 32, 1, KH> {
 template <>
 struct EdgeLoop<__nv_bfloat16, 8, 32, 1, -1> {
   using type = Agg<__nv_bfloat16, 8, 32, 1>;
+};
+template <int KH>
+struct EdgeLoop<float, 4, 32, 2, KH> {
+  using type = AggFast32<KH>;
+};
+template <>
+struct EdgeLoop<float, 4, 32, 2, -1> {
+  using type = Agg<float, 4, 32, 2>;
 };
 template <int KH>
 struct EdgeLoop<__nv_bfloat16, 8, 8, 1, KH> {
@@ -1122,6 +1243,17 @@ int run_aggregate(gnnc_ctx_t* ctx, const Launch& L, AggParams p) {
       case 2: fn = agg_kernel<__nv_bfloat16, 8, 8, 1, 2>; break;
       case 4: fn = agg_kernel<__nv_bfloat16, 8, 8, 1, 4>; break;
       case 8: fn = agg_kernel<__nv_bfloat16, 8, 8, 1, 8>; break;
+      default: break;
+    }
+  }
+  if (!fn && L.h_dtype == GNNC_F32 && vec == 4 && p.F == 256) {
+    // fp32 rows of 256: specialised loop for a compile-time head count
+    switch (p.mode == MODE_GCN ? 0 : p.H) {
+      case 0: fn = agg_kernel<float, 4, 32, 2, 0>; break;
+      case 1: fn = agg_kernel<float, 4, 32, 2, 1>; break;
+      case 2: fn = agg_kernel<float, 4, 32, 2, 2>; break;
+      case 4: fn = agg_kernel<float, 4, 32, 2, 4>; break;
+      case 8: fn = agg_kernel<float, 4, 32, 2, 8>; break;
       default: break;
     }
   }

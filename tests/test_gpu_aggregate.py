@@ -205,13 +205,14 @@ def test_bad_column_is_skipped_and_reported(device):
     rt.Context.get(device).synchronize()  # flag cleared
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("H,C,concat", [(1, 256, True), (2, 128, True), (8, 32, True),
                                          (4, 64, False), (3, 256, True)])
-def test_gat_bf16_256_wide_head_counts(device, H, C, concat):
-    """bf16 rows of 256 features (one 16-byte load per lane) for every head
-    count the compile-time edge loops cover, a mean-over-heads epilogue, and
-    a width that takes the generic loop (3 x 256 features)."""
-    out, ref, _ = _gat_case(device, 1800, 30000, H, C, torch.bfloat16, ((4, 7000), (6, 900)), 0,
+def test_gat_256_wide_head_counts(device, H, C, concat, dtype):
+    """Rows of 256 features (bf16: one 16-byte load per lane; fp32: two) for
+    every head count the compile-time edge loops cover, a mean-over-heads
+    epilogue, and a width that takes the generic loop (3 x 256 features)."""
+    out, ref, _ = _gat_case(device, 1800, 30000, H, C, dtype, ((4, 7000), (6, 900)), 0,
                             0, concat, act=2, lsm=False, seed=40 + H)
     assert_close(out, ref)
 
