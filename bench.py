@@ -226,6 +226,101 @@ def broadcast_workload(rank, world, device, scale=1.0):
 # ---------------------------------------------------------------------------
 
 
+class NeededExchange:
+    """Layer on `world` ranks moving only the remote input rows this rank's
+    edges read (partition.NeededRows): each owner packs, per requester, the
+    rows it needs into one block of its exported pack buffer (gnnc_gather_rows);
+    each requester pulls one block per owner with the copy engines into its
+    compact table, pipelined with the projection; the local CSR's columns are
+    relabelled to compact-table rows. Three one-word NCCL all-reduces per step
+    order the owners' input writes, their packs and the peers' reads."""
+
+    PIECE_ROWS = 1 << 18
+
+    def __init__(self, P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device):
+        N = x_d.size(0)
+        self.P, self.rt, self.N = P, rt, N
+        self.rr = rr = P.row_range(N, world, rank)
+        rowptr_l, col_l = P.local_csr(rowptr, col, rr)
+        self.need = need = P.NeededRows(col_l, rr)
+        self.rowptr_l, self.col_l = rowptr_l, need.col
+        self.n_loc = rr.count
+        self.ld = ld = rt.row_stride(IN, torch.bfloat16)
+        R = rr.rows_per_rank
+        self.x_own = torch.zeros((R, ld), dtype=torch.bfloat16, device=device)
+        self.x_own[: rr.count, :IN] = x_d[rr.begin : rr.end]
+        self.pack = torch.zeros((max(1, need.pack_rows), ld), dtype=torch.bfloat16, device=device)
+        self.peers = P.PeerBuffers(self.pack)
+        nc = need.compact_rows
+        self.xc = torch.zeros((max(1, nc - R), ld), dtype=torch.bfloat16, device=device)
+        self.h_full = rt.empty_rows(nc, F, torch.bfloat16, device)
+        self.a_full = torch.empty((nc, HEADS), dtype=torch.float32, device=device)
+        self.d_own = torch.empty((R, HEADS), dtype=torch.float32, device=device)
+        self.adst_l = self.d_own[: rr.count]
+        self.n_src = nc
+        self.W, self.att_s, self.att_d = W, att_s, att_d
+        self.fence_buf = torch.zeros(1, dtype=torch.int32, device=device)
+        self.pieces = []
+        for p in P.read_order(rr)[1:]:
+            n_p = need.need_rows[p]
+            for a in range(0, n_p, self.PIECE_ROWS):
+                self.pieces.append((p, a, min(n_p, a + self.PIECE_ROWS)))
+        self.side = torch.cuda.Stream(device)
+        self.piece_ev = [torch.cuda.Event() for _ in self.pieces]
+        self.proj_launches = 1 + len(self.pieces) + 1  # projections + the pack
+        remote = max(1, N - rr.count)
+        self.describe = (f"owners pack, requesters pull only the remote input rows their edges "
+                         f"read ({sum(need.need_rows) / remote:.0%} of the remote rows here) over "
+                         "NVLink with the copy engines (CUDA IPC), pipelined with the projection")
+
+    def x_local_rows(self):
+        return self.x_own[: self.n_loc, :IN]
+
+    def node_ids(self):
+        return torch.arange(self.rr.begin, self.rr.end)
+
+    def fence(self):
+        dist.all_reduce(self.fence_buf)
+
+    def _proj(self, x, rows: slice, adst):
+        self.rt.proj(x, self.W, att_src=self.att_s, att_dst=self.att_d, heads=HEADS,
+                     out_dtype=torch.bfloat16, out=self.h_full[rows], asrc_out=self.a_full[rows],
+                     adst_out=adst)
+
+    def project(self):
+        need, rt, R = self.need, self.rt, self.rr.rows_per_rank
+        self.fence()  # every rank's input rows are written
+        if need.pack_rows:
+            rt.gather_rows(self.x_own, need.pack_idx, self.pack)
+        self.fence()  # every rank's packs are written
+        cur = torch.cuda.current_stream()
+        self.side.wait_stream(cur)
+        row_bytes = self.ld * 2
+        with torch.cuda.stream(self.side):
+            for (p, a, b), ev in zip(self.pieces, self.piece_ev):
+                off = need.remote_off[p]
+                rt.peer_copy(self.xc[need.base[p] - R + a :], self.peers.rows(p, off + a, off + b),
+                             (b - a) * row_bytes)
+                ev.record(self.side)
+        n = self.n_loc
+        self._proj(self.x_own[:n, :IN], slice(0, n), self.d_own[:n])
+        for (p, a, b), ev in zip(self.pieces, self.piece_ev):
+            cur.wait_event(ev)
+            lo = need.base[p] + a
+            xs = self.xc[lo - R : lo - R + (b - a), :IN]
+            # a_dst of remote rows is not used: it goes to a scratch buffer
+            self._proj(xs, slice(lo, lo + (b - a)), self._dscratch(b - a))
+        self.fence()  # every rank is done reading the packs
+
+    def _dscratch(self, rows):
+        if getattr(self, "_ds", None) is None or self._ds.size(0) < rows:
+            self._ds = torch.empty((rows, HEADS), dtype=torch.float32, device=self.x_own.device)
+        return self._ds[:rows]
+
+    def close(self):
+        self.peers.close()
+
+
 class PeerExchange:
     """Layer on `world` ranks reading the remote input rows from the owners'
     HBM: rank r owns rows [r*R, (r+1)*R) and their input rows; every rank maps
@@ -257,6 +352,7 @@ class PeerExchange:
         self.a_full = torch.empty((world * R, HEADS), dtype=torch.float32, device=device)
         self.d_full = torch.empty((world * R, HEADS), dtype=torch.float32, device=device)
         self.adst_l = self.d_full[rr.begin : rr.begin + rr.count]
+        self.n_src = N
         self.W, self.att_s, self.att_d = W, att_s, att_d
         self.fence_buf = torch.zeros(1, dtype=torch.int32, device=device)
         self.order = P.read_order(rr)
@@ -276,6 +372,9 @@ class PeerExchange:
 
     def x_local_rows(self):
         return self.x_own[: self.n_loc, :IN]
+
+    def node_ids(self):
+        return torch.arange(self.rr.begin, self.rr.end)
 
     def fence(self):
         dist.all_reduce(self.fence_buf)
@@ -332,6 +431,7 @@ class InputExchange:
         self.a_full = torch.empty((rb.padded_rows, HEADS), dtype=torch.float32, device=device)
         self.d_full = torch.empty((rb.padded_rows, HEADS), dtype=torch.float32, device=device)
         self.adst_l = torch.empty((rb.count, HEADS), dtype=torch.float32, device=device)
+        self.n_src = N
         self.W, self.att_s, self.att_d = W, att_s, att_d
         self.comm = torch.cuda.Stream(device) if world > 1 else None
         self.piece_ev = [torch.cuda.Event() for _ in range(chunks)]
@@ -341,6 +441,9 @@ class InputExchange:
 
     def x_local_rows(self):
         return self.x_loc[: self.n_loc, :IN]
+
+    def node_ids(self):
+        return self.rb.node_ids()
 
     def project(self):
         rb, P, rt = self.rb, self.P, self.rt
@@ -380,12 +483,16 @@ class OutputExchange:
         self.h_full = P.gathered_table(rr, F, torch.bfloat16, device)
         self.a_full = P.gathered_table(rr, HEADS, torch.float32, device)
         self.adst_l = torch.empty((rr.count, HEADS), dtype=torch.float32, device=device)
+        self.n_src = N
         self.W, self.att_s, self.att_d = W, att_s, att_d
         self.proj_launches = 1
         self.describe = "NCCL all-gather of h and a_src"
 
     def x_local_rows(self):
         return self.X_l
+
+    def node_ids(self):
+        return torch.arange(self.rr.begin, self.rr.end)
 
     def project(self):
         rr, P = self.rr, self.P
@@ -423,13 +530,16 @@ def run_b200(args) -> None:
     att_d = conv.att_dst.detach().reshape(-1).to(device)
     bias = conv.bias.detach().to(device)
     chunks = args.chunks or (1 if world == 1 else 4)
-    if args.exchange == "peer" and world > 1:
+    if args.exchange == "needed" and world > 1:
+        lay = NeededExchange(P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device)
+    elif args.exchange == "peer" and world > 1:
         lay = PeerExchange(P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device,
                            read=args.peer_read)
     elif args.exchange in ("input", "peer"):
         lay = InputExchange(P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, chunks, device)
     else:
         lay = OutputExchange(P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device)
+    full = (rowptr, col, x_d) if args.check else None
     del rowptr, col, x_d
     rowptr_l, col_l = lay.rowptr_l, lay.col_l
     n_loc, e_loc = lay.n_loc, col_l.numel()
@@ -439,7 +549,8 @@ def run_b200(args) -> None:
     project = lay.project
 
     def aggregate():
-        rt.gat_aggregate(plan, rowptr_l, col_l, lay.h_full[:N], lay.a_full[:N], lay.adst_l,
+        rt.gat_aggregate(plan, rowptr_l, col_l, lay.h_full[: lay.n_src], lay.a_full[: lay.n_src],
+                         lay.adst_l,
                          heads=HEADS, concat=True, bias=bias, act=rt.ACT_ELU,
                          out_dtype=torch.bfloat16, out=out_l)
 
@@ -488,6 +599,12 @@ def run_b200(args) -> None:
     worst = int(g[:, 1].argmax())
     agg_worst, bytes_worst = float(g[worst, 1]), float(g[worst, 3])
 
+    check = None
+    if args.check:
+        check = check_rows(rt, lay, full, W, att_s, att_d, bias, out_l, device)
+        log(f"[bench] rank {rank}: own rows vs the single-GPU layer: {check}")
+        full = None
+
     # ---- end to end through the public API (host buffers, copies timed) ----
     e2e = None
     if not args.no_e2e:
@@ -525,6 +642,7 @@ def run_b200(args) -> None:
                 "parallelism": f"dst-row partition x{world}" + (f" + {lay.describe}" if world > 1 else ""),
                 "l2": "inputs larger than L2 (h table 1.25 GB, X 0.51 GB; L2 126 MB): no flush",
                 "exchange": args.exchange if world > 1 else None,
+                "check": check,
                 "chunks": chunks if world > 1 else None,
                 "plan": info,
             },
@@ -707,6 +825,23 @@ def run_c5(args) -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def check_rows(rt, lay, full, W, att_s, att_d, bias, out_l, device) -> str:
+    """This rank's output rows against the same layer computed on this GPU alone
+    (all rows projected, the whole CSR aggregated): "bit-exact" or "MISMATCH"."""
+    from gnnc.b200.program import to_device_features
+
+    rowptr, col, x_d = full
+    N = x_d.size(0)
+    X = to_device_features(x_d, torch.bfloat16, device)
+    h, a, d = rt.proj(X, W, att_src=att_s, att_dst=att_d, heads=HEADS, out_dtype=torch.bfloat16)
+    out = rt.gat_aggregate(rt.Plan(rowptr), rowptr, col, h, a, d, heads=HEADS, concat=True,
+                           bias=bias, act=rt.ACT_ELU, out_dtype=torch.bfloat16)
+    ids = lay.node_ids().to(device)
+    same = torch.equal(out[ids].contiguous(), out_l.contiguous())
+    del N
+    return "bit-exact" if same else "MISMATCH"
 
 
 def e2e_b200(args, layer, ei_host, x_host, device, world, N, E, project, aggregate, lay, out_l):
@@ -909,7 +1044,7 @@ def main() -> None:
                     help="the headline layer (default) or the c5 fused-aggregation microbenchmark")
     ap.add_argument("--cta-threshold", type=int, default=0)
     ap.add_argument("--split-threshold", type=int, default=0)
-    ap.add_argument("--exchange", default="peer", choices=("peer", "input", "output"),
+    ap.add_argument("--exchange", default="peer", choices=("peer", "needed", "input", "output"),
                     help="N>1: read remote input rows in the projection (default), "
                          "all-gather the input X, or all-gather the projected h")
     ap.add_argument("--peer-read", default="copy", choices=("copy", "tma"),
@@ -920,6 +1055,8 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--ref-step-seconds", type=float, default=0.3)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--check", action="store_true",
+                    help="compare each rank's output rows with the single-GPU layer (bit-exact)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--scale", type=float, default=1.0,

@@ -294,6 +294,15 @@ GNNC_API int gnnc_peer_open(gnnc_ctx_t* ctx, const void* handle, uint64_t offset
 GNNC_API int gnnc_peer_copy(gnnc_ctx_t* ctx, void* dst, const void* src, size_t bytes);
 GNNC_API int gnnc_peer_close(gnnc_ctx_t* ctx, void* ptr, uint64_t offset);
 
+/* dst[i] = src[idx[i]] for i < n: rows of row_bytes bytes, strides in bytes,
+ * all 16-byte aligned. Packs the rows another rank needs into one contiguous
+ * block that it then pulls with one gnnc_peer_copy. An index outside
+ * [0, n_src) leaves its row untouched and is reported as GNNC_ERR_BOUNDS by
+ * the next gnnc_synchronize. No reference counterpart (multi-GPU exchange). */
+GNNC_API int gnnc_gather_rows(gnnc_ctx_t* ctx, const void* src, int64_t ld_src,
+                              const int32_t* idx, int64_t n, int64_t n_src, void* dst,
+                              int64_t ld_dst, int64_t row_bytes);
+
 #ifdef __cplusplus
 }
 #endif

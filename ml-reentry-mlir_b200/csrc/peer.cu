@@ -34,9 +34,53 @@ GetAddressRangeFn range_fn(gnnc_ctx_t* ctx) {
   return g_range;
 }
 
+// One warp per destination row: dst[i] = src[idx[i]] (row_bytes bytes, 16-byte
+// chunks). An index outside [0, n_src) leaves the row alone and raises the
+// context's bad-index word (reported by gnnc_synchronize).
+__global__ void gather_rows_kernel(const char* __restrict__ src, int64_t ld_src,
+                                   const int32_t* __restrict__ idx, int64_t n, int64_t n_src,
+                                   char* __restrict__ dst, int64_t ld_dst, int64_t chunks,
+                                   int* bad) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x / 32);
+  for (int64_t i = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) / 32; i < n; i += warps) {
+    const int32_t r = __ldg(idx + i);
+    if (r < 0 || r >= n_src) {
+      if (lane == 0) atomicOr(bad, 1);
+      continue;
+    }
+    const uint4* s = reinterpret_cast<const uint4*>(src + int64_t(r) * ld_src);
+    uint4* d = reinterpret_cast<uint4*>(dst + i * ld_dst);
+    for (int64_t c = lane; c < chunks; c += 32) d[c] = __ldg(s + c);
+  }
+}
+
 }  // namespace
 
 extern "C" {
+
+int gnnc_gather_rows(gnnc_ctx_t* ctx, const void* src, int64_t ld_src, const int32_t* idx,
+                     int64_t n, int64_t n_src, void* dst, int64_t ld_dst, int64_t row_bytes) {
+  if (!ctx) return GNNC_ERR_INVALID;
+  GNNC_CHECK_ARG(ctx, n >= 0 && n_src >= 0 && row_bytes > 0, "bad sizes");
+  GNNC_CHECK_ARG(ctx, n == 0 || (src && idx && dst), "null argument");
+  GNNC_CHECK_ARG(ctx, row_bytes % 16 == 0 && ld_src % 16 == 0 && ld_dst % 16 == 0 &&
+                          reinterpret_cast<uintptr_t>(src) % 16 == 0 &&
+                          reinterpret_cast<uintptr_t>(dst) % 16 == 0,
+                 "rows, strides and pointers must be 16-byte aligned");
+  GNNC_CHECK_ARG(ctx, ld_src >= row_bytes && ld_dst >= row_bytes, "stride below row size");
+  if (n == 0) return GNNC_OK;
+  GNNC_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  const int64_t want = (n + 7) / 8;
+  const int64_t cap = int64_t(ctx->num_sms) * 8;
+  const unsigned grid = unsigned(want < cap ? want : cap);
+  gather_rows_kernel<<<grid, 256, 0, ctx->stream>>>(
+      static_cast<const char*>(src), ld_src, idx, n, n_src, static_cast<char*>(dst), ld_dst,
+      row_bytes / 16, ctx->dev_words + 2);
+  GNNC_CUDA_TRY(ctx, cudaGetLastError());
+  return GNNC_OK;
+}
+
 
 int gnnc_peer_export(gnnc_ctx_t* ctx, const void* ptr, void* handle, uint64_t* offset) {
   if (!ctx) return GNNC_ERR_INVALID;

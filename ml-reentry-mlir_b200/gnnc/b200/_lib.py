@@ -79,6 +79,7 @@ SIGNATURES: dict[str, tuple] = {
     "gnnc_peer_open": (c_int, [_P, _P, ctypes.c_uint64, POINTER(c_void_p)]),
     "gnnc_peer_close": (c_int, [_P, _P, ctypes.c_uint64]),
     "gnnc_peer_copy": (c_int, [_P, _P, _P, c_size_t]),
+    "gnnc_gather_rows": (c_int, [_P, _P, _I64, _P, _I64, _I64, _P, _I64, _I64]),
     "gnnc_gat_aggregate_noalloc": (
         c_int,
         [

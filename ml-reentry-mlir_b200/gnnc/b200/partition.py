@@ -264,3 +264,103 @@ def read_order(rr: RowRange) -> list[int]:
     """Owners in the order a rank reads them: itself first, then the next
     ranks cyclically, so that at any moment the ranks read different peers."""
     return [(rr.rank + k) % rr.world for k in range(rr.world)]
+
+
+# ---------------------------------------------------------------------------
+# needed rows: only the remote rows a rank's edges read cross NVLink
+# ---------------------------------------------------------------------------
+
+
+class NeededRows:
+    """Which remote input rows a rank's edges read, and how they travel.
+
+    With contiguous row ranges, rank r's edges read the rows of every other
+    rank p, but on a power-law graph only a part of them (about two thirds of
+    the remote rows at 8 ranks on the 2.45M-node configuration-model graph).
+    need[p] lists them (sorted offsets into p's rows). The ranks swap these
+    lists once; then, per forward:
+
+    * as owner, a rank packs for each requester q the rows q needs into one
+      contiguous block of its pack buffer (`pack_idx`, block q at
+      `pack_off[q]`), so a requester pulls one block per owner;
+    * as requester, a rank lands owner p's block at rows `base[p]` of its
+      compact table, whose first R rows are its own;
+    * `col` is the local CSR's column array relabelled to compact-table rows.
+    """
+
+    def __init__(self, col_l: torch.Tensor, rr: RowRange, group=None) -> None:
+        import torch.distributed as dist
+
+        R, W, me = rr.rows_per_rank, rr.world, rr.rank
+        dev = col_l.device
+        c = col_l.long()
+        uniq = torch.unique(c)
+        owner = uniq // R
+        need = [(uniq[owner == p] - p * R).to(torch.int32) for p in range(W)]
+        need[me] = need[me][:0]
+        lists: list = [None] * W
+        dist.all_gather_object(lists, [t.cpu() for t in need], group=group)
+        send = [lists[q][me] if q != me else torch.empty(0, dtype=torch.int32) for q in range(W)]
+        sizes = [int(t.numel()) for t in send]
+        self.pack_off = [sum(sizes[:q]) for q in range(W)]
+        self.pack_rows = sum(sizes)
+        self.pack_idx = (torch.cat(send).to(dev) if self.pack_rows
+                         else torch.empty(0, dtype=torch.int32, device=dev))
+        offs: list = [None] * W
+        dist.all_gather_object(offs, self.pack_off, group=group)
+        self.remote_off = [offs[p][me] for p in range(W)]  # my block in p's pack buffer
+        self.need_rows = [int(t.numel()) for t in need]
+        self.base = [0] * W
+        nxt = R
+        for p in read_order(rr)[1:]:
+            self.base[p] = nxt
+            nxt += self.need_rows[p]
+        self.compact_rows = nxt
+        comp = torch.empty_like(c)
+        src_owner = c // R
+        mine = src_owner == me
+        comp[mine] = c[mine] - me * R
+        for p in range(W):
+            if p == me or not self.need_rows[p]:
+                continue
+            m = src_owner == p
+            comp[m] = self.base[p] + torch.searchsorted(need[p].long(), c[m] - p * R)
+        self.col = comp.to(torch.int32).contiguous()
+        self.rr = rr
+
+
+class PeerBuffers:
+    """Every rank's copy of a row buffer (rows may differ per rank, the row
+    stride may not), mapped into this process over CUDA IPC; rows(p, a, b)
+    addresses rows [a, b) of rank p's buffer."""
+
+    def __init__(self, local: torch.Tensor, group=None) -> None:
+        import torch.distributed as dist
+
+        from gnnc.b200 import runtime as rt
+
+        self._rt, self.local = rt, local
+        world, me = dist.get_world_size(group), dist.get_rank(group)
+        meta: list = [None] * world
+        dist.all_gather_object(meta, rt.peer_export(local), group=group)
+        self.ptrs: list[int] = []
+        self._opened: list[tuple[int, int]] = []
+        for p in range(world):
+            if p == me:
+                self.ptrs.append(local.data_ptr())
+            else:
+                handle, off = meta[p]
+                ptr = rt.peer_open(local.device, handle, off)
+                self._opened.append((ptr, off))
+                self.ptrs.append(ptr)
+
+    def rows(self, p: int, a: int, b: int):
+        t = self.local
+        rb = t.stride(0) * t.element_size()
+        return self._rt.DeviceRows(self.ptrs[p] + a * rb, b - a, t.size(1), t.stride(0), t.dtype,
+                                   t.device)
+
+    def close(self) -> None:
+        for ptr, off in self._opened:
+            self._rt.peer_close(self.local.device, ptr, off)
+        self._opened = []

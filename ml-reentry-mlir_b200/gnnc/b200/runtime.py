@@ -31,6 +31,7 @@ __all__ = [
     "gat_aggregate",
     "gat_aggregate_noalloc",
     "gcn_aggregate",
+    "gather_rows",
     "gcn_norm",
     "mean_norm",
     "peer_close",
@@ -613,6 +614,24 @@ def peer_copy(dst: torch.Tensor | DeviceRows, src: torch.Tensor | DeviceRows, nb
         if nbytes > cap:
             raise ValueError(f"{name} holds {cap} bytes, {nbytes} requested")
     Context.get(dev).call("gnnc_peer_copy", ptr["dst"], ptr["src"], nbytes)
+
+
+def gather_rows(src: torch.Tensor, idx: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out[i] = src[idx[i]] (whole padded rows; 16-byte aligned row strides)."""
+    _check_cuda(src, idx, out)
+    if idx.dtype != torch.int32 or not idx.is_contiguous():
+        raise ValueError("idx must be a contiguous int32 tensor")
+    n = idx.numel()
+    if out.size(0) < n or out.dtype != src.dtype:
+        raise ValueError("out must hold len(idx) rows of src's dtype")
+    esz = src.element_size()
+    row_bytes = src.stride(0) * esz
+    if out.stride(0) * esz < row_bytes:
+        raise ValueError("out rows are narrower than src rows")
+    Context.get(src.device).call("gnnc_gather_rows", src.data_ptr(), src.stride(0) * esz,
+                                 idx.data_ptr(), n, src.size(0), out.data_ptr(),
+                                 out.stride(0) * esz, row_bytes)
+    return out
 
 
 def peer_close(device: torch.device | int, ptr: int, offset: int) -> None:

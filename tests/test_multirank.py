@@ -177,3 +177,50 @@ def test_peer_read_order_starts_local_and_spreads_owners():
         # at every position k of the read sequence the ranks read distinct owners
         for k in range(world):
             assert len({o[k] for o in orders}) == world
+
+
+def _rank_needed(rank, world, port, out_dir):
+    sys.path[:0] = [ROOT, os.path.join(ROOT, "ml-reentry-mlir_b200")]
+    import torch.distributed as dist
+
+    from gnnc.b200 import partition as P
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world)
+    rowptr, col, x, W, a_s, a_d, H, C = _problem()
+    n = x.size(0)
+    rr = P.row_range(n, world, rank)
+    rowptr_l, col_l = P.local_csr(rowptr, col, rr)
+    plan = P.NeededRows(col_l.to(torch.int32), rr)
+    R = rr.rows_per_rank
+    x_own = torch.zeros(R, x.size(1), dtype=x.dtype)
+    x_own[: rr.count] = x[rr.begin : rr.end]
+    packed = x_own[plan.pack_idx.long()]  # the owner-side pack
+    blocks: list = [None] * world
+    dist.all_gather_object(blocks, packed)  # stands in for the peer pulls
+    table = torch.zeros(plan.compact_rows, x.size(1), dtype=x.dtype)
+    table[:R] = x_own
+    for p in range(world):
+        if p != rank and plan.need_rows[p]:
+            off = plan.remote_off[p]
+            table[plan.base[p] : plan.base[p] + plan.need_rows[p]] = blocks[p][off : off + plan.need_rows[p]]
+    ok = torch.equal(table[plan.col.long()], x[col_l.long()])
+    frac = sum(plan.need_rows) / max(1, n - rr.count)
+    torch.save({"ok": ok, "frac": frac}, os.path.join(out_dir, f"n{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.timeout(180)
+def test_needed_rows_relabel_and_offsets_gloo(tmp_path):
+    """Three ranks: each packs the rows the others need, the blocks travel
+    (all_gather here, peer pulls on the GPU), and the compact table indexed by
+    the relabelled columns gives every edge its source row."""
+    import torch.multiprocessing as mp
+
+    world = 3
+    mp.spawn(_rank_needed, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    for r in range(world):
+        got = torch.load(tmp_path / f"n{r}.pt")
+        assert got["ok"]
+        assert 0.0 < got["frac"] <= 1.0
