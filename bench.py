@@ -533,6 +533,8 @@ def run_b200(args) -> None:
     if args.exchange == "needed" and world > 1:
         lay = NeededExchange(P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device)
     elif args.exchange == "peer" and world > 1:
+        if args.piece_rows:
+            PeerExchange.PIECE_ROWS = args.piece_rows
         lay = PeerExchange(P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device,
                            read=args.peer_read)
     elif args.exchange in ("input", "peer"):
@@ -1047,6 +1049,8 @@ def main() -> None:
     ap.add_argument("--exchange", default="peer", choices=("peer", "needed", "input", "output"),
                     help="N>1: read remote input rows in the projection (default), "
                          "all-gather the input X, or all-gather the projected h")
+    ap.add_argument("--piece-rows", type=int, default=0,
+                    help="peer exchange: rows per pulled piece (default 2^18)")
     ap.add_argument("--peer-read", default="copy", choices=("copy", "tma"),
                     help="peer exchange: copy-engine staging (default) or direct TMA reads")
     ap.add_argument("--chunks", type=int, default=0,
