@@ -55,6 +55,19 @@ def _time_forward(lowered, inputs, warmup: int, iters: int) -> dict:
         torch.cuda.synchronize(dev)
         cur = [(a.elapsed_time(b), b.elapsed_time(c)) for a, b, c in evs]
         per = cur if per is None else [(min(p0, c0), min(p1, c1)) for (p0, p1), (c0, c1) in zip(per, cur)]
+    # the same forward replayed from a captured CUDA graph (small graphs)
+    graph_ms = None
+    if lowered._replay(xd, gd) is not None:
+        for _ in range(warmup):
+            lowered._replay(xd, gd)
+        torch.cuda.synchronize(dev)
+        s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(iters):
+            lowered._replay(xd, gd)
+        e0.record()
+        torch.cuda.synchronize(dev)
+        graph_ms = s0.elapsed_time(e0) / iters
     edges = lowered.graph_edges(gd, x.size(0))
     layers = [
         {"layer": i + 1, "proj_ms": pj, "agg_ms": ag, "edges": e, "agg_edges_per_s": e / (ag / 1e3),
@@ -62,7 +75,7 @@ def _time_forward(lowered, inputs, warmup: int, iters: int) -> dict:
         for i, ((pj, ag), e) in enumerate(zip(per, edges))
     ]
     return {"median_ms": ms[len(ms) // 2], "p90_ms": ms[int(len(ms) * 0.9)], "iters": iters,
-            "layers": layers}
+            "cuda_graph_ms": graph_ms, "layers": layers}
 
 
 def _relaunch(argv: list[str], gpus: int) -> int:
@@ -238,6 +251,8 @@ def main(argv: list[str] | None = None) -> int:
     actual = outs[0].cpu().numpy()
     if timing:
         print(f"  forward  : median {timing['median_ms']:.3f} ms, p90 {timing['p90_ms']:.3f} ms")
+        if timing["cuda_graph_ms"] is not None:
+            print(f"  forward  : {timing['cuda_graph_ms']:.3f} ms replayed from a CUDA graph (mean)")
         for lay in timing["layers"]:
             print(f"  layer {lay['layer']}  : proj {lay['proj_ms']:.3f} ms, agg {lay['agg_ms']:.3f} ms, "
                   f"{lay['edges']} edges, {lay['agg_edges_per_s'] / 1e9:.2f} G edges/s (agg), "
