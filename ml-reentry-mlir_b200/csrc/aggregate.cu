@@ -1220,22 +1220,12 @@ struct Launch {
   int64_t ldh;
 };
 
-int run_aggregate(gnnc_ctx_t* ctx, const Launch& L, AggParams p) {
-  const gnnc_plan_t* plan = L.plan;
-  // Vector width: 16-byte loads when the row stride, base pointer and (for
-  // multi-head softmax) the head width allow it; scalar loads otherwise.
-  const int vmax = L.h_dtype == GNNC_BF16 ? 8 : 4;
-  const bool heads_ok = (p.mode == MODE_GCN) || p.H == 1 || (p.C % vmax == 0);
-  const bool align_ok = (reinterpret_cast<uintptr_t>(L.h) % 16 == 0) && (L.ldh % vmax == 0);
-  const int vec = (heads_ok && align_ok) ? vmax : 1;
-  int lpg, nv;
-  row_layout(p.F, vec, &lpg, &nv);
-  if (nv > 8)
-    return gnnc::set_error(ctx, GNNC_ERR_UNSUPPORTED,
-                           "feature width %d too large for the row kernel (vector width %d)", p.F,
-                           vec);
+// The aggregation kernel for a layout: the specialised edge loops where they
+// apply (compile-time head counts for 256-wide bf16 / fp32 rows and narrow
+// bf16 rows), the generic template otherwise; nullptr if there is none.
+KernelFn choose_kernel(const AggParams& p, int h_dtype, int vec, int lpg, int nv) {
   KernelFn fn = nullptr;
-  if (L.h_dtype == GNNC_BF16 && vec == 8 && lpg == 8 && nv == 1) {
+  if (h_dtype == GNNC_BF16 && vec == 8 && lpg == 8 && nv == 1) {
     // Narrow rows (32 < F <= 64): specialised loop for a compile-time head count.
     switch (p.mode == MODE_GCN ? 0 : p.H) {
       case 0: fn = agg_kernel<__nv_bfloat16, 8, 8, 1, 0>; break;
@@ -1246,7 +1236,7 @@ int run_aggregate(gnnc_ctx_t* ctx, const Launch& L, AggParams p) {
       default: break;
     }
   }
-  if (!fn && L.h_dtype == GNNC_F32 && vec == 4 && p.F == 256) {
+  if (!fn && h_dtype == GNNC_F32 && vec == 4 && p.F == 256) {
     // fp32 rows of 256: specialised loop for a compile-time head count
     switch (p.mode == MODE_GCN ? 0 : p.H) {
       case 0: fn = agg_kernel<float, 4, 32, 2, 0>; break;
@@ -1257,7 +1247,7 @@ int run_aggregate(gnnc_ctx_t* ctx, const Launch& L, AggParams p) {
       default: break;
     }
   }
-  if (!fn && L.h_dtype == GNNC_BF16 && vec == 8 && p.F == 256) {
+  if (!fn && h_dtype == GNNC_BF16 && vec == 8 && p.F == 256) {
     // Specialised edge loop for a compile-time head count. It reads a_src
     // rows (or score rows) as one vector: they must be aligned to it.
     const int kh = p.mode == MODE_GCN ? 0 : p.H;
@@ -1272,12 +1262,27 @@ int run_aggregate(gnnc_ctx_t* ctx, const Launch& L, AggParams p) {
       default: break;
     }
   }
-  if (fn) {
-    // specialised loop chosen
-  } else if (L.h_dtype == GNNC_BF16)
-    fn = vec == 8 ? pick_layout<__nv_bfloat16, 8>(lpg, nv) : pick_layout<__nv_bfloat16, 1>(lpg, nv);
-  else
-    fn = vec == 4 ? pick_layout<float, 4>(lpg, nv) : pick_layout<float, 1>(lpg, nv);
+  if (fn) return fn;
+  if (h_dtype == GNNC_BF16)
+    return vec == 8 ? pick_layout<__nv_bfloat16, 8>(lpg, nv) : pick_layout<__nv_bfloat16, 1>(lpg, nv);
+  return vec == 4 ? pick_layout<float, 4>(lpg, nv) : pick_layout<float, 1>(lpg, nv);
+}
+
+int run_aggregate(gnnc_ctx_t* ctx, const Launch& L, AggParams p) {
+  const gnnc_plan_t* plan = L.plan;
+  // Vector width: 16-byte loads when the row stride, base pointer and (for
+  // multi-head softmax) the head width allow it; scalar loads otherwise.
+  const int vmax = L.h_dtype == GNNC_BF16 ? 8 : 4;
+  const bool heads_ok = (p.mode == MODE_GCN) || p.H == 1 || (p.C % vmax == 0);
+  const bool align_ok = (reinterpret_cast<uintptr_t>(L.h) % 16 == 0) && (L.ldh % vmax == 0);
+  const int vec = (heads_ok && align_ok) ? vmax : 1;
+  int lpg, nv;
+  row_layout(p.F, vec, &lpg, &nv);
+  if (nv > 8)
+    return gnnc::set_error(ctx, GNNC_ERR_UNSUPPORTED,
+                           "feature width %d too large for the row kernel (vector width %d)", p.F,
+                           vec);
+  KernelFn fn = choose_kernel(p, L.h_dtype, vec, lpg, nv);
   if (!fn) return gnnc::set_error(ctx, GNNC_ERR_UNSUPPORTED, "no kernel for layout");
 
   p.F_pad = int(gnnc::align_up(size_t(lpg * vec * nv), 4));
@@ -1285,11 +1290,12 @@ int run_aggregate(gnnc_ctx_t* ctx, const Launch& L, AggParams p) {
   p.fast_epilogue = fast_epilogue_ok(p, vec);
   p.part_stride = part_stride_floats(p.F_pad);
   p.cta_items = plan->cta_items;
-  p.n_cta_items = plan->n_cta_items;
+  const bool wide = lpg == 32;  // a whole warp per edge
+  p.n_cta_items = wide ? plan->n_cta_items_wide : plan->n_cta_items;
   p.split_rows = plan->split_rows;
   p.warp_tasks = plan->warp_tasks;
   p.n_warp_tasks = plan->n_warp_tasks;
-  p.cta_threshold = plan->cta_threshold;
+  p.cta_threshold = wide ? plan->wide_threshold : plan->cta_threshold;
   p.counters = ctx->dev_words;
   p.partials = nullptr;
   if (plan->n_segments > 0) {
@@ -1359,9 +1365,16 @@ extern "C" int gnnc_plan_create(gnnc_ctx_t* ctx, const int32_t* rowptr, int64_t 
   *out_plan = nullptr;
   GNNC_CHECK_ARG(ctx, n_rows >= 0 && n_rows < (int64_t(1) << 31), "bad n_rows");
   GNNC_CHECK_ARG(ctx, rowptr != nullptr, "null rowptr");
+  const bool default_cta = cta_threshold <= 0;
   if (cta_threshold <= 0) cta_threshold = 256;
   if (split_threshold <= 0) split_threshold = 4096;
   GNNC_CHECK_ARG(ctx, split_threshold >= cta_threshold, "split_threshold < cta_threshold");
+  // With the default thresholds, launches on wide rows (256 features: a whole
+  // warp per edge) give rows of up to 1024 edges to the warp path, which is
+  // faster there than the CTA path (measured on the c4 graph); narrow rows
+  // keep the CTA path from 257 edges up.
+  const int wide_threshold =
+      default_cta ? std::min(1024, split_threshold) : cta_threshold;
   GNNC_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
   std::vector<int32_t> rp(size_t(n_rows) + 1);
   GNNC_CUDA_TRY(ctx, cudaMemcpyAsync(rp.data(), rowptr, rp.size() * sizeof(int32_t),
@@ -1399,7 +1412,7 @@ extern "C" int gnnc_plan_create(gnnc_ctx_t* ctx, const int32_t* rowptr, int64_t 
     } else if (deg > cta_threshold) {
       items.push_back(make_int4(int(r), rp[r], rp[r + 1], -1));
       ++n_cta;
-      cost += 1;
+      cost += deg <= wide_threshold ? deg + kRowCost : 1;
     } else {
       ++n_warp;
       cost += deg + kRowCost;
@@ -1410,9 +1423,16 @@ extern "C" int gnnc_plan_create(gnnc_ctx_t* ctx, const int32_t* rowptr, int64_t 
     }
   }
   if (tasks.back() != n_rows) tasks.push_back(int32_t(n_rows));
-  // Largest CTA items first, so the long ones do not form the tail.
-  std::stable_sort(items.begin(), items.end(),
-                   [](const int4& a, const int4& b) { return (a.z - a.y) > (b.z - b.y); });
+  // Largest CTA items first, so the long ones do not form the tail; whole
+  // rows the wide launches leave to warps go last.
+  auto warp_on_wide = [&](const int4& it) { return it.w < 0 && it.z - it.y <= wide_threshold; };
+  std::stable_sort(items.begin(), items.end(), [&](const int4& a, const int4& b) {
+    const bool wa = warp_on_wide(a), wb = warp_on_wide(b);
+    if (wa != wb) return wb;
+    return (a.z - a.y) > (b.z - b.y);
+  });
+  int64_t n_items_wide = 0;
+  for (const int4& it : items) n_items_wide += warp_on_wide(it) ? 0 : 1;
 
   gnnc_plan_t* plan = new gnnc_plan_t();
   plan->n_rows = n_rows;
@@ -1423,6 +1443,8 @@ extern "C" int gnnc_plan_create(gnnc_ctx_t* ctx, const int32_t* rowptr, int64_t 
   plan->n_split_rows = int64_t(splits.size());
   plan->n_segments = n_seg;
   plan->n_cta_items = int64_t(items.size());
+  plan->wide_threshold = wide_threshold;
+  plan->n_cta_items_wide = n_items_wide;
   plan->n_warp_tasks = int64_t(tasks.size()) - 1;
   plan->max_degree = max_deg;
   plan->device = ctx->device;
@@ -1662,7 +1684,7 @@ extern "C" int gnnc_gat_aggregate_noalloc(gnnc_ctx_t* ctx, const gnnc_plan_t* pl
   p.slope = negative_slope; p.eps = 1e-16f; p.bias = bias; p.out = out; p.out_dtype = out_dtype;
   p.ldo = ldo;
 
-  // Same kernel choice as gnnc_gat_aggregate.
+  // Same kernel choice as gnnc_gat_aggregate (choose_kernel).
   const int vmax = h_dtype == GNNC_BF16 ? 8 : 4;
   const bool heads_ok = p.H == 1 || (p.C % vmax == 0);
   const bool align_ok = (reinterpret_cast<uintptr_t>(h) % 16 == 0) && (ldh % vmax == 0);
@@ -1673,22 +1695,19 @@ extern "C" int gnnc_gat_aggregate_noalloc(gnnc_ctx_t* ctx, const gnnc_plan_t* pl
     return gnnc::set_error(ctx, GNNC_ERR_UNSUPPORTED,
                            "feature width %d too large for the row kernel (vector width %d)", p.F,
                            vec);
-  KernelFn fn = nullptr;
-  if (h_dtype == GNNC_BF16)
-    fn = vec == 8 ? pick_layout<__nv_bfloat16, 8>(lpg, nv) : pick_layout<__nv_bfloat16, 1>(lpg, nv);
-  else
-    fn = vec == 4 ? pick_layout<float, 4>(lpg, nv) : pick_layout<float, 1>(lpg, nv);
+  KernelFn fn = choose_kernel(p, h_dtype, vec, lpg, nv);
   if (!fn) return gnnc::set_error(ctx, GNNC_ERR_UNSUPPORTED, "no kernel for layout");
   p.F_pad = int(gnnc::align_up(size_t(lpg * vec * nv), 4));
   p.HS = head_stride(p.mode, p.H);
   p.fast_epilogue = fast_epilogue_ok(p, vec);
   p.part_stride = part_stride_floats(p.F_pad);
   p.cta_items = plan->cta_items;
-  p.n_cta_items = plan->n_cta_items;
+  const bool wide = lpg == 32;  // a whole warp per edge
+  p.n_cta_items = wide ? plan->n_cta_items_wide : plan->n_cta_items;
   p.split_rows = plan->split_rows;
   p.warp_tasks = plan->warp_tasks;
   p.n_warp_tasks = plan->n_warp_tasks;
-  p.cta_threshold = plan->cta_threshold;
+  p.cta_threshold = wide ? plan->wide_threshold : plan->cta_threshold;
 
   const size_t need = size_t(plan->n_segments) * p.part_stride * sizeof(float);
   if (need > kStaticScratchBytes - kStaticCounterBytes)

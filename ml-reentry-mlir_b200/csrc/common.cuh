@@ -35,6 +35,11 @@ struct gnnc_plan {
   int64_t n_split_rows = 0;    // rows cut into several CTA segments
   int64_t n_segments = 0;      // partial slots used by split rows
   int64_t n_cta_items = 0;     // CTA work items (cta rows + segments)
+  // Rows of up to wide_threshold edges go to the warp path when the rows are
+  // wide (a whole warp per edge): their CTA items are the last ones, and
+  // launches on wide rows process only the first n_cta_items_wide items.
+  int wide_threshold = 256;
+  int64_t n_cta_items_wide = 0;
   int64_t n_warp_tasks = 0;    // contiguous row ranges for the warp path
   int max_degree = 0;
   int device = 0;
