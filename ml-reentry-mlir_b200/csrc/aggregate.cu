@@ -1366,6 +1366,7 @@ extern "C" int gnnc_plan_create(gnnc_ctx_t* ctx, const int32_t* rowptr, int64_t 
   GNNC_CHECK_ARG(ctx, n_rows >= 0 && n_rows < (int64_t(1) << 31), "bad n_rows");
   GNNC_CHECK_ARG(ctx, rowptr != nullptr, "null rowptr");
   const bool default_cta = cta_threshold <= 0;
+  const bool default_split = split_threshold <= 0;
   if (cta_threshold <= 0) cta_threshold = 256;
   if (split_threshold <= 0) split_threshold = 4096;
   GNNC_CHECK_ARG(ctx, split_threshold >= cta_threshold, "split_threshold < cta_threshold");
@@ -1387,6 +1388,15 @@ extern "C" int gnnc_plan_create(gnnc_ctx_t* ctx, const int32_t* rowptr, int64_t 
       return gnnc::set_error(ctx, GNNC_ERR_BOUNDS, "rowptr decreases at row %lld",
                              (long long)r);
 
+  if (default_split) {
+    // Split a row across CTAs only when one CTA alone would take a sizeable
+    // share of the launch: longer than the edges per resident CTA over two
+    // (at least 4096). Splitting costs partials and a merge launch; on the c4
+    // graph (max degree 6,853) no row needs it, on the scale-24 R-MAT graph
+    // the hub rows of ~370k edges do.
+    const int64_t per = (int64_t(rp[size_t(n_rows)]) - rp[0]) / (2 * int64_t(ctx->num_sms) * 4);
+    split_threshold = int(std::min<int64_t>(std::max<int64_t>(4096, per), int64_t(1) << 30));
+  }
   std::vector<int4> items, splits;
   std::vector<int32_t> tasks;
   int64_t n_warp = 0, n_cta = 0, n_seg = 0;
