@@ -96,3 +96,25 @@ def test_peer_export_rejects_host_memory(device):
     assert st == _lib.ERR_INVALID
     with pytest.raises(ValueError):
         rt.peer_export(torch.zeros(4))
+
+
+def test_gather_rows_packs_whole_rows(device):
+    """gnnc_gather_rows: dst[i] = src[idx[i]], padded rows copied whole; an
+    index past the table is skipped and reported by the next synchronize."""
+    from gnnc.b200 import runtime as rt
+    from gnnc.b200._lib import GnncInvalidArgument
+
+    src = rt.empty_rows(1000, 100, torch.bfloat16, device)
+    src.copy_(torch.randn(1000, 100, device=device))
+    base = src.as_strided((1000, src.stride(0)), (src.stride(0), 1))
+    idx = torch.randint(0, 1000, (777,), device=device, dtype=torch.int32)
+    out = torch.zeros((777, src.stride(0)), dtype=torch.bfloat16, device=device)
+    rt.gather_rows(base, idx, out)
+    assert torch.equal(out, base[idx.long()])
+    bad = torch.tensor([3, 5000, 7], device=device, dtype=torch.int32)
+    out2 = torch.zeros((3, src.stride(0)), dtype=torch.bfloat16, device=device)
+    rt.gather_rows(base, bad, out2)
+    with pytest.raises(GnncInvalidArgument):
+        rt.Context.get(device).synchronize()
+    assert torch.equal(out2[0], base[3]) and torch.equal(out2[2], base[7])
+    assert bool((out2[1] == 0).all())
