@@ -17,6 +17,13 @@ download, from the same places under DATA_DIR, and rebuild the same tensors:
   (one "source,target" per line, kept directed as OGB does for this dataset),
   node-feat.csv.gz (128 floats per line) and node-label.csv.gz: 169,343 nodes,
   1,166,243 edges, 40 classes.
+* ogbn-products (OGB raw layout, DATA_DIR/ogb/ogbn_products/raw/): the same
+  three files; each undirected edge is stored once, and OGB's loader (its
+  dataset table sets add_inverse_edge for this dataset) puts the reverse
+  right after each stored edge: (u, v), (v, u), ... in file order. 2,449,029
+  nodes, 61,859,140 directed edges, 100 features, 47 classes -- the graph whose
+  shapes the synthetic c4 workload reproduces. The reference ships no loader
+  for it (its dataset pre-download script leaves it for later).
 
 Nothing is downloaded: a missing file raises DatasetNotFound (a ValueError,
 so gnnc-bench exits with code 2) naming the path to put it at.
@@ -31,7 +38,7 @@ from pathlib import Path
 import numpy as np
 import torch
 
-__all__ = ["DatasetNotFound", "load", "load_cora", "load_ogbn_arxiv"]
+__all__ = ["DatasetNotFound", "load", "load_cora", "load_ogbn_arxiv", "load_ogbn_products"]
 
 
 class DatasetNotFound(ValueError):
@@ -92,18 +99,31 @@ def _read_csv_gz(path: Path, dtype) -> np.ndarray:
         return np.loadtxt(f, delimiter=",", dtype=dtype, ndmin=2)
 
 
-def load_ogbn_arxiv(root: Path):
-    """(x [N, 128] float32, edge_index [2, E] int64, y [N] int64, num_classes)."""
-    raw = Path(root) / "ogb" / "ogbn_arxiv" / "raw"
-    edges = _read_csv_gz(raw / "edge.csv.gz", np.int64)
+def _load_ogb(root: Path, name: str, add_inverse: bool):
+    raw = Path(root) / "ogb" / name / "raw"
+    edges = _read_csv_gz(raw / "edge.csv.gz", np.int64)  # [E0, 2]
     x = torch.from_numpy(_read_csv_gz(raw / "node-feat.csv.gz", np.float32))
     y = torch.from_numpy(_read_csv_gz(raw / "node-label.csv.gz", np.int64)).reshape(-1)
+    if add_inverse:  # (u, v) then (v, u) for every stored edge, in file order
+        edges = np.stack([edges, edges[:, ::-1]], axis=1).reshape(-1, 2)
     edge_index = torch.from_numpy(np.ascontiguousarray(edges.T))
     return x, edge_index, y, int(y.max()) + 1
 
 
+def load_ogbn_arxiv(root: Path):
+    """(x [N, 128] float32, edge_index [2, E] int64, y [N] int64, num_classes)."""
+    return _load_ogb(root, "ogbn_arxiv", add_inverse=False)
+
+
+def load_ogbn_products(root: Path):
+    """(x [N, 100] float32, edge_index [2, 2*E0] int64 with both directions of
+    every stored edge, y [N] int64, num_classes)."""
+    return _load_ogb(root, "ogbn_products", add_inverse=True)
+
+
 def load(name: str, root: Path | None = None):
-    """(x, edge_index, y, num_classes) of "cora" or "ogbn-arxiv" from DATA_DIR."""
+    """(x, edge_index, y, num_classes) of "cora", "ogbn-arxiv" or "ogbn-products"
+    from DATA_DIR."""
     if root is None:
         from gnnc.paths import DATA_DIR
 
@@ -112,4 +132,6 @@ def load(name: str, root: Path | None = None):
         return load_cora(root)
     if name == "ogbn-arxiv":
         return load_ogbn_arxiv(root)
+    if name == "ogbn-products":
+        return load_ogbn_products(root)
     raise ValueError(f"unknown dataset: {name}")

@@ -4,8 +4,9 @@
 (gnnc/ingress.py:25-49): load the model file, take inputs from its own
 get_inputs()/get_init_inputs() or from a named dataset, seed 0, build the model.
 Named datasets are the reference's real ones ("cora", "ogbn-arxiv", loaded
-through PyG/OGB when installed) and the seeded synthetic workloads of
-gnnc.examples.synthetic ("c1" ... "c5"). The torch-mlir import
+through PyG/OGB when installed), "ogbn-products" (the real graph behind the c4
+shapes) and the seeded synthetic workloads of gnnc.examples.synthetic
+("c1" ... "c5"). The torch-mlir import
 (import_as_raw_ir) belongs to the MLIR targets and is not part of this build.
 """
 
@@ -67,7 +68,7 @@ def _dataset_inputs(model_name: str, dataset: str):
     from gnnc.examples.util import normalized_csr_adj
     from gnnc.paths import DATA_DIR
 
-    if dataset not in ("cora", "ogbn-arxiv"):
+    if dataset not in ("cora", "ogbn-arxiv", "ogbn-products"):
         return synthetic_inputs(model_name, dataset)
     try:  # the reference's loaders, when PyG / OGB are installed
         if dataset == "cora":
@@ -77,7 +78,7 @@ def _dataset_inputs(model_name: str, dataset: str):
         else:
             from ogb.nodeproppred import PygNodePropPredDataset
 
-            ds = PygNodePropPredDataset(name="ogbn-arxiv", root=str(DATA_DIR / "ogb"))
+            ds = PygNodePropPredDataset(name=dataset, root=str(DATA_DIR / "ogb"))
     except ImportError:  # the same raw files, read without them
         from gnnc.datasets import load
 

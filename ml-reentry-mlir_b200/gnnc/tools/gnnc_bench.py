@@ -180,7 +180,7 @@ def main(argv: list[str] | None = None) -> int:
     )
     parser.add_argument("--model", required=True, choices=available())
     parser.add_argument("--dataset", "--config", default=None,
-                        help="cora | ogbn-arxiv | c1 | c2 | c3 | c3-bf16 | c4; omit for get_inputs()")
+                        help="cora | ogbn-arxiv | ogbn-products | c1 | c2 | c3 | c3-bf16 | c4; omit for get_inputs()")
     parser.add_argument("--gpus", type=int, default=1,
                         help="P > 1: row-partitioned forward on P GPUs (one process each)")
     parser.add_argument("--target", default="b200", choices=("b200", "cpu", "gpu"))

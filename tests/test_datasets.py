@@ -53,22 +53,41 @@ def test_planetoid_raw_files(tmp_path):
     assert ei.tolist() == [[a for a, _ in pairs], [b for _, b in pairs]]
 
 
-def test_ogb_raw_files(tmp_path):
-    from gnnc.datasets import load_ogbn_arxiv
-
-    raw = tmp_path / "ogb" / "ogbn_arxiv" / "raw"
+def _write_ogb(root, name, seed=1):
+    raw = root / "ogb" / name / "raw"
     raw.mkdir(parents=True)
-    rng = np.random.default_rng(1)
+    rng = np.random.default_rng(seed)
     edges = rng.integers(0, 7, (11, 2))
     feat = rng.standard_normal((7, 4)).astype(np.float32)
     label = rng.integers(0, 5, (7, 1))
-    for name, arr, fmt in (("edge", edges, "%d"), ("node-feat", feat, "%.8e"),
-                           ("node-label", label, "%d")):
-        with gzip.open(raw / f"{name}.csv.gz", "wt") as f:
+    for fname, arr, fmt in (("edge", edges, "%d"), ("node-feat", feat, "%.8e"),
+                            ("node-label", label, "%d")):
+        with gzip.open(raw / f"{fname}.csv.gz", "wt") as f:
             np.savetxt(f, arr, delimiter=",", fmt=fmt)
+    return edges, feat, label
+
+
+def test_ogb_raw_files(tmp_path):
+    from gnnc.datasets import load_ogbn_arxiv
+
+    edges, feat, label = _write_ogb(tmp_path, "ogbn_arxiv")
     x, ei, y, nc = load_ogbn_arxiv(tmp_path)
     assert np.array_equal(ei.numpy(), edges.T) and np.allclose(x.numpy(), feat)
     assert np.array_equal(y.numpy(), label.reshape(-1)) and nc == int(label.max()) + 1
+
+
+def test_ogbn_products_adds_the_reverse_of_each_edge(tmp_path):
+    """Stored edges are undirected: each (u, v) is followed by (v, u)."""
+    from gnnc.datasets import load
+
+    edges, feat, label = _write_ogb(tmp_path, "ogbn_products", seed=2)
+    x, ei, y, nc = load("ogbn-products", tmp_path)
+    want = []
+    for u, v in edges.tolist():
+        want += [(u, v), (v, u)]
+    assert ei.t().tolist() == [list(p) for p in want]
+    assert np.allclose(x.numpy(), feat) and np.array_equal(y.numpy(), label.reshape(-1))
+    assert nc == int(label.max()) + 1
 
 
 def test_missing_files_name_the_path(tmp_path):
@@ -78,6 +97,8 @@ def test_missing_files_name_the_path(tmp_path):
         load("cora", tmp_path)
     with pytest.raises(ValueError):
         load("ogbn-arxiv", tmp_path)
+    with pytest.raises(DatasetNotFound, match="ogbn_products"):
+        load("ogbn-products", tmp_path)
 
 
 def test_ingress_reads_the_raw_files(tmp_path, monkeypatch):
@@ -91,3 +112,15 @@ def test_ingress_reads_the_raw_files(tmp_path, monkeypatch):
     model, (x, adj) = get_model_and_data(MODELS_DIR / "gcn.py", "cora")
     assert adj.layout == torch.sparse_csr and adj.size(0) == x.size(0) == 9
     assert model.conv1.lin.weight.size(1) == x.size(1)
+
+
+def test_ingress_reads_ogbn_products_for_gat(tmp_path, monkeypatch):
+    """gnnc-bench --model gat --dataset ogbn-products: edge_index with both directions."""
+    import gnnc.paths
+    from gnnc.examples import MODELS_DIR
+    from gnnc.ingress import get_model_and_data
+
+    edges, feat, _ = _write_ogb(tmp_path, "ogbn_products", seed=3)
+    monkeypatch.setattr(gnnc.paths, "DATA_DIR", tmp_path)
+    model, (x, ei) = get_model_and_data(MODELS_DIR / "gat.py", "ogbn-products")
+    assert ei.shape == (2, 2 * len(edges)) and x.shape == feat.shape
