@@ -12,14 +12,17 @@
 //   warp 1: allocates 512 TMEM columns (two 128 x 256 fp32 accumulators); one
 //     lane issues tcgen05.mma (M = 128, N = F16, K = 16 per instruction) and
 //     tcgen05.commit to release stages and publish finished tiles.
-//   warps 2-9: epilogue. Warp w reads TMEM lanes 32*(w%4) .. +31 (one tile
-//     row per thread) and the column half (w-2)/4 of the accumulator (halves
-//     split at a multiple of 128 bytes of output and, for GAT, at a head
-//     boundary). Per 128-byte pass of its columns it folds the per-head dot
+//   warps 2-17: epilogue, four warps per scheduler (the epilogue is a chain
+//     of dependent TMEM loads, FMAs and conversions: it needs the warps to
+//     hide that latency). Warp w reads TMEM lanes 32*(w%4) .. +31 (one tile
+//     row per thread) and the column group (w-2)/4 of the accumulator (four
+//     groups, split at multiples of 128 bytes of output and, for GAT, at head
+//     boundaries). Per 128-byte pass of its columns it folds the per-head dot
 //     products with att_src / att_dst (fixed summation order: deterministic),
 //     converts, writes the values into a 128-byte-swizzled staging box and
-//     hands the box to a TMA bulk-tensor store (two boxes per warp in
-//     flight). The store clips rows >= N and columns >= F.
+//     hands the box to a TMA bulk-tensor store (one box per warp: at F = 256
+//     bf16 a warp makes one pass per tile, so the box it reuses was handed
+//     off a whole tile earlier). The store clips rows >= N and columns >= F.
 // The two accumulators let the MMAs of tile i+1 run under the epilogue of
 // tile i. Every mbarrier wait is bounded by %globaltimer; a wait that gives up
 // raises an abort flag the other roles see, records GNNC_ERR_TIMEOUT in the
@@ -38,25 +41,26 @@ constexpr int kBK = 64;   // k-block: 64 bf16 = one 128-byte swizzle row
 constexpr int kStagesResident = 5;  // x-only stages when w stays resident
 constexpr int kStagesStream = 3;    // x + w stages otherwise
 constexpr int kMaxStages = 5;
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 16;
+constexpr int kEpiGroups = kEpiWarps / 4;  // column groups (4 TMEM lane quarters each)
 constexpr int kThreads = (2 + kEpiWarps) * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccStride = 256;  // TMEM columns per accumulator buffer
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s per wait
 constexpr int kMaxF = 256;
 constexpr int kResidentWBytes = 64 * 1024;
-// Output staging: one TMA store box = 32 rows x 128 bytes, two per epilogue
-// warp (1024-byte aligned: the 128-byte swizzle repeats every 8 rows).
+// Output staging: one TMA store box = 32 rows x 128 bytes per epilogue warp
+// (1024-byte aligned: the 128-byte swizzle repeats every 8 rows).
 constexpr int kBoxRows = 32;
 constexpr int kBoxBytes = kBoxRows * 128;
-constexpr int kStagingBytes = kEpiWarps * 2 * kBoxBytes;
+constexpr int kStagingBytes = kEpiWarps * kBoxBytes;
 // Bytes reserved for the 2*kMaxStages + 6 mbarriers (a multiple of 16).
 constexpr int kBarrierBytes = ((2 * kMaxStages + 6) * 8 + 15) / 16 * 16;
 static_assert(kBarrierBytes % 16 == 0 && kBoxBytes % 1024 == 0, "aligned regions");
 
 struct TcParams {
   int N, K, F, N16, nkb, n_tiles;
-  int cs;  // accumulator columns per epilogue half
+  int cs;  // accumulator columns per epilogue column group
   int Fs;  // columns the bulk stores cover: F rounded down to 16 bytes of output
   int w_resident;  // all w k-blocks live in shared memory for the whole kernel
   int stages;
@@ -146,9 +150,9 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
 __device__ __forceinline__ void bulk_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
-// Waits until at most one committed store group still reads shared memory.
-__device__ __forceinline__ void bulk_wait_read_1() {
-  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+// Waits until no committed store group still reads shared memory.
+__device__ __forceinline__ void bulk_wait_read_0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
@@ -254,35 +258,38 @@ __device__ __forceinline__ void att_flush(const TcParams& p, int64_t row, int hd
   }
 }
 
-// One 128-byte pass of an epilogue warp over W accumulator columns from c0 of
-// this thread's row (TMEM lane): attention partial sums of the heads the
-// columns belong to, conversion into the swizzled staging box (16-byte chunk
-// j of row r at chunk slot j ^ (r % 8)), and the TMA store of the box.
-template <int W, bool kBf16>
-__device__ __forceinline__ void epi_pass(const TcParams& p, const CUtensorMap* map_h,
-                                         uint32_t taddr, int c0, int64_t row, int row0,
-                                         unsigned char* box, const float* s_att, bool att,
-                                         float (&ps)[4], float (&pd)[4], int& cur, int lane) {
-  static_assert(W % 16 == 0 && W <= (kBf16 ? 64 : 32), "one 128-byte pass");
-  uint32_t r[W];
-#pragma unroll
-  for (int off = 0; off + 32 <= W; off += 32) tmem_ld32_async(taddr + uint32_t(c0 + off), r + off);
-  if constexpr (W % 32 != 0) tmem_ld16_async(taddr + uint32_t(c0 + W - 16), r + W - 16);
+// One block of WB (32 or 16) accumulator columns from column c of this
+// thread's row (TMEM lane): attention partial sums of the heads the columns
+// belong to, then conversion into the row's slot of the swizzled staging box
+// (16-byte chunk j of row r at chunk slot j ^ (r % 8); jbase = the block's
+// first chunk within the 128-byte row). Blocks are loaded and retired one at a
+// time so a thread holds at most 32 accumulator columns.
+template <int WB, bool kBf16>
+__device__ __forceinline__ void epi_block(const TcParams& p, uint32_t taddr, int c, int jbase,
+                                          unsigned char* srow, const float* s_att, bool att,
+                                          int64_t row, float (&ps)[4], float (&pd)[4], int& cur,
+                                          int lane) {
+  static_assert(WB == 32 || WB == 16, "block width");
+  uint32_t r[WB];
+  if constexpr (WB == 32)
+    tmem_ld32_async(taddr + uint32_t(c), r);
+  else
+    tmem_ld16_async(taddr + uint32_t(c), r);
   tmem_wait_ld();
   if (att) {
 #pragma unroll
-    for (int sub = 0; sub < W; sub += 16) {
-      const int c = c0 + sub;
+    for (int sub = 0; sub < WB; sub += 16) {
+      const int cc = c + sub;
       // A 16-column chunk lies in one head (C % 16 == 0 or H == 1).
-      const int hd = p.H == 1 ? 0 : c / p.C;
+      const int hd = p.H == 1 ? 0 : cc / p.C;
       if (hd != cur) {
         if (cur >= 0) att_flush(p, row, cur, ps, pd);
 #pragma unroll
         for (int j = 0; j < 4; ++j) ps[j] = pd[j] = 0.f;
         cur = hd;
       }
-      const float4* ws = reinterpret_cast<const float4*>(s_att + c);
-      const float4* wd = reinterpret_cast<const float4*>(s_att + kMaxF + c);
+      const float4* ws = reinterpret_cast<const float4*>(s_att + cc);
+      const float4* wd = reinterpret_cast<const float4*>(s_att + kMaxF + cc);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float4 a = ws[j], d = wd[j];
@@ -295,8 +302,7 @@ __device__ __forceinline__ void epi_pass(const TcParams& p, const CUtensorMap* m
       }
     }
   }
-  unsigned char* srow = box + lane * 128;
-  constexpr int kChunks = kBf16 ? W / 8 : W / 4;
+  constexpr int kChunks = kBf16 ? WB / 8 : WB / 4;
 #pragma unroll
   for (int j = 0; j < kChunks; ++j) {
     uint4 v;
@@ -309,8 +315,28 @@ __device__ __forceinline__ void epi_pass(const TcParams& p, const CUtensorMap* m
     } else {
       v = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
     }
-    *reinterpret_cast<uint4*>(srow + ((j ^ (lane & 7)) << 4)) = v;
+    *reinterpret_cast<uint4*>(srow + (((jbase + j) ^ (lane & 7)) << 4)) = v;
   }
+}
+
+// One 128-byte pass of an epilogue warp over W accumulator columns from c0 of
+// this thread's row: the blocks of epi_block, the partial last chunk, and the
+// TMA store of the staging box.
+template <int W, bool kBf16>
+__device__ __forceinline__ void epi_pass(const TcParams& p, const CUtensorMap* map_h,
+                                         uint32_t taddr, int c0, int64_t row, int row0,
+                                         unsigned char* box, const float* s_att, bool att,
+                                         float (&ps)[4], float (&pd)[4], int& cur, int lane) {
+  static_assert(W % 16 == 0 && W <= (kBf16 ? 64 : 32), "one 128-byte pass");
+  constexpr int kColsPerChunk = kBf16 ? 8 : 4;
+  unsigned char* srow = box + lane * 128;
+#pragma unroll
+  for (int b = 0; b + 32 <= W; b += 32)
+    epi_block<32, kBf16>(p, taddr, c0 + b, b / kColsPerChunk, srow, s_att, att, row, ps, pd, cur,
+                         lane);
+  if constexpr (W % 32 != 0)
+    epi_block<16, kBf16>(p, taddr, c0 + W - 16, (W - 16) / kColsPerChunk, srow, s_att, att, row,
+                         ps, pd, cur, lane);
   // Columns [Fs, F) end in a partial 16-byte chunk, which a bulk store would
   // write whole: this thread stores them from its staged chunk instead.
   if (p.Fs < p.F && p.Fs >= c0 && p.Fs < c0 + W && row < p.N) {
@@ -465,14 +491,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(drain, 0, abort, false);
     }
   } else {
-    // Epilogue: TMEM lanes 32*(warp%4) .. +31, column half (warp-2)/4.
+    // Epilogue: TMEM lanes 32*(warp%4) .. +31, column group (warp-2)/4.
     const int q = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const int c_begin = half * p.cs;
+    const int group = (warp - 2) >> 2;
+    const int c_begin = group * p.cs;
     const int c_end = min(p.N16, c_begin + p.cs);
     const int pass_cols = p.h_bf16 ? 64 : 32;  // 128 bytes of output per row
-    unsigned char* boxes = s_stage + (warp - 2) * 2 * kBoxBytes;
-    int t_iter = 0, pass_no = 0;
+    unsigned char* box = s_stage + (warp - 2) * kBoxBytes;
+    int t_iter = 0;
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++t_iter) {
       const int b = t_iter & 1;
       if (!mbar_wait(&tfull[b], (t_iter >> 1) & 1, abort)) break;
@@ -482,11 +508,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t row = int64_t(row0) + lane;
       float ps[4] = {0.f, 0.f, 0.f, 0.f}, pd[4] = {0.f, 0.f, 0.f, 0.f};
       int cur = -1;
-      for (int c0 = c_begin; c0 < c_end; c0 += pass_cols, ++pass_no) {
+      for (int c0 = c_begin; c0 < c_end; c0 += pass_cols) {
         const int width = min(pass_cols, c_end - c0);
-        unsigned char* box = boxes + (pass_no & 1) * kBoxBytes;
-        // the store that last read this box (two passes ago) is done reading
-        if (lane == 0) bulk_wait_read_1();
+        // the store that last read this box (the previous pass) is done reading
+        if (lane == 0) bulk_wait_read_0();
         __syncwarp();
         if (p.h_bf16) {
           switch (width) {
@@ -599,9 +624,9 @@ int proj_tc_try(gnnc_ctx_t* ctx, const void* x, int64_t ldx, const void* w, int6
                 h_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                 h_esize))
     return kProjTcDeclined;
-  // Column split between the two epilogue halves: about half the columns,
-  // rounded up to whole 128-byte passes and, with attention, to whole heads
-  // (a head's dot products stay in one warp).
+  // Column split between the epilogue's column groups: about a quarter of the
+  // columns each, rounded up to whole 128-byte passes and, with attention, to
+  // whole heads (a head's dot products stay in one warp).
   int unit = pass_cols;
   if (att && H > 1) {
     const int c = int(C);
@@ -611,7 +636,7 @@ int proj_tc_try(gnnc_ctx_t* ctx, const void* x, int64_t ldx, const void* w, int6
   } else if (att) {
     unit = N16;
   }
-  int cs = ((N16 + 1) / 2 + unit - 1) / unit * unit;
+  int cs = ((N16 + kEpiGroups - 1) / kEpiGroups + unit - 1) / unit * unit;
   if (cs < unit) cs = unit;
 
   TcParams p{};
