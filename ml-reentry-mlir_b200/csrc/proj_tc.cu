@@ -30,6 +30,7 @@
 // frees TMEM before the kernel returns.
 #include <cuda.h>  // CUtensorMap and the cuTensorMapEncodeTiled prototype (no libcuda link)
 
+#include <climits>
 #include <mutex>
 
 #include "proj_tc.cuh"
@@ -249,6 +250,19 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
 }
 
+// (c0, c1) += (a0 * b0, a1 * b1) as one packed fp32x2 FMA: each lane rounds
+// exactly as fmaf does.
+__device__ __forceinline__ void ffma2(float& c0, float& c1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%0, %1};\n\t"
+      "fma.rn.f32x2 rc, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rc;\n\t}"
+      : "+f"(c0), "+f"(c1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 // Flushes the attention sums of head `hd` for this thread's row.
 __device__ __forceinline__ void att_flush(const TcParams& p, int64_t row, int hd, const float (&ps)[4],
                                           const float (&pd)[4]) {
@@ -263,12 +277,15 @@ __device__ __forceinline__ void att_flush(const TcParams& p, int64_t row, int hd
 // belong to, then conversion into the row's slot of the swizzled staging box
 // (16-byte chunk j of row r at chunk slot j ^ (r % 8); jbase = the block's
 // first chunk within the 128-byte row). Blocks are loaded and retired one at a
-// time so a thread holds at most 32 accumulator columns.
+// time so a thread holds at most 32 accumulator columns. `cur` is the head
+// whose sums ps / pd hold and `head_end` its first column past the head;
+// columns arrive in increasing order, so crossing head_end moves to the next
+// head (a 16-column chunk never straddles two: C % 16 == 0 or H == 1).
 template <int WB, bool kBf16>
 __device__ __forceinline__ void epi_block(const TcParams& p, uint32_t taddr, int c, int jbase,
                                           unsigned char* srow, const float* s_att, bool att,
                                           int64_t row, float (&ps)[4], float (&pd)[4], int& cur,
-                                          int lane) {
+                                          int& head_end, int lane) {
   static_assert(WB == 32 || WB == 16, "block width");
   uint32_t r[WB];
   if constexpr (WB == 32)
@@ -280,13 +297,12 @@ __device__ __forceinline__ void epi_block(const TcParams& p, uint32_t taddr, int
 #pragma unroll
     for (int sub = 0; sub < WB; sub += 16) {
       const int cc = c + sub;
-      // A 16-column chunk lies in one head (C % 16 == 0 or H == 1).
-      const int hd = p.H == 1 ? 0 : cc / p.C;
-      if (hd != cur) {
-        if (cur >= 0) att_flush(p, row, cur, ps, pd);
+      if (cc >= head_end) {
+        att_flush(p, row, cur, ps, pd);
 #pragma unroll
         for (int j = 0; j < 4; ++j) ps[j] = pd[j] = 0.f;
-        cur = hd;
+        ++cur;
+        head_end += p.C;
       }
       const float4* ws = reinterpret_cast<const float4*>(s_att + cc);
       const float4* wd = reinterpret_cast<const float4*>(s_att + kMaxF + cc);
@@ -295,10 +311,10 @@ __device__ __forceinline__ void epi_block(const TcParams& p, uint32_t taddr, int
         const float4 a = ws[j], d = wd[j];
         const float v0 = __uint_as_float(r[sub + 4 * j]), v1 = __uint_as_float(r[sub + 4 * j + 1]);
         const float v2 = __uint_as_float(r[sub + 4 * j + 2]), v3 = __uint_as_float(r[sub + 4 * j + 3]);
-        ps[0] = fmaf(v0, a.x, ps[0]); ps[1] = fmaf(v1, a.y, ps[1]);
-        ps[2] = fmaf(v2, a.z, ps[2]); ps[3] = fmaf(v3, a.w, ps[3]);
-        pd[0] = fmaf(v0, d.x, pd[0]); pd[1] = fmaf(v1, d.y, pd[1]);
-        pd[2] = fmaf(v2, d.z, pd[2]); pd[3] = fmaf(v3, d.w, pd[3]);
+        ffma2(ps[0], ps[1], v0, v1, a.x, a.y);
+        ffma2(ps[2], ps[3], v2, v3, a.z, a.w);
+        ffma2(pd[0], pd[1], v0, v1, d.x, d.y);
+        ffma2(pd[2], pd[3], v2, v3, d.z, d.w);
       }
     }
   }
@@ -326,17 +342,18 @@ template <int W, bool kBf16>
 __device__ __forceinline__ void epi_pass(const TcParams& p, const CUtensorMap* map_h,
                                          uint32_t taddr, int c0, int64_t row, int row0,
                                          unsigned char* box, const float* s_att, bool att,
-                                         float (&ps)[4], float (&pd)[4], int& cur, int lane) {
+                                         float (&ps)[4], float (&pd)[4], int& cur, int& head_end,
+                                         int lane) {
   static_assert(W % 16 == 0 && W <= (kBf16 ? 64 : 32), "one 128-byte pass");
   constexpr int kColsPerChunk = kBf16 ? 8 : 4;
   unsigned char* srow = box + lane * 128;
 #pragma unroll
   for (int b = 0; b + 32 <= W; b += 32)
     epi_block<32, kBf16>(p, taddr, c0 + b, b / kColsPerChunk, srow, s_att, att, row, ps, pd, cur,
-                         lane);
+                         head_end, lane);
   if constexpr (W % 32 != 0)
     epi_block<16, kBf16>(p, taddr, c0 + W - 16, (W - 16) / kColsPerChunk, srow, s_att, att, row,
-                         ps, pd, cur, lane);
+                         ps, pd, cur, head_end, lane);
   // Columns [Fs, F) end in a partial 16-byte chunk, which a bulk store would
   // write whole: this thread stores them from its staged chunk instead.
   if (p.Fs < p.F && p.Fs >= c0 && p.Fs < c0 + W && row < p.N) {
@@ -498,6 +515,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int c_end = min(p.N16, c_begin + p.cs);
     const int pass_cols = p.h_bf16 ? 64 : 32;  // 128 bytes of output per row
     unsigned char* box = s_stage + (warp - 2) * kBoxBytes;
+    // The group starts on a head boundary (the host splits at whole heads).
+    const bool multi_head = att && p.H > 1;
+    const int hd0 = multi_head ? c_begin / p.C : 0;
+    const int head_end0 = multi_head ? (hd0 + 1) * p.C : INT_MAX;
     int t_iter = 0;
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++t_iter) {
       const int b = t_iter & 1;
@@ -507,7 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row0 = tile * kBM + q * 32;
       const int64_t row = int64_t(row0) + lane;
       float ps[4] = {0.f, 0.f, 0.f, 0.f}, pd[4] = {0.f, 0.f, 0.f, 0.f};
-      int cur = -1;
+      int cur = hd0, head_end = head_end0;
       for (int c0 = c_begin; c0 < c_end; c0 += pass_cols) {
         const int width = min(pass_cols, c_end - c0);
         // the store that last read this box (the previous pass) is done reading
@@ -515,19 +536,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (p.h_bf16) {
           switch (width) {
-            case 64: epi_pass<64, true>(p, &map_h, taddr, c0, row, row0, box, s_att, att, ps, pd, cur, lane); break;
-            case 48: epi_pass<48, true>(p, &map_h, taddr, c0, row, row0, box, s_att, att, ps, pd, cur, lane); break;
-            case 32: epi_pass<32, true>(p, &map_h, taddr, c0, row, row0, box, s_att, att, ps, pd, cur, lane); break;
-            default: epi_pass<16, true>(p, &map_h, taddr, c0, row, row0, box, s_att, att, ps, pd, cur, lane); break;
+            case 64: epi_pass<64, true>(p, &map_h, taddr, c0, row, row0, box, s_att, att, ps, pd, cur, head_end, lane); break;
+            case 48: epi_pass<48, true>(p, &map_h, taddr, c0, row, row0, box, s_att, att, ps, pd, cur, head_end, lane); break;
+            case 32: epi_pass<32, true>(p, &map_h, taddr, c0, row, row0, box, s_att, att, ps, pd, cur, head_end, lane); break;
+            default: epi_pass<16, true>(p, &map_h, taddr, c0, row, row0, box, s_att, att, ps, pd, cur, head_end, lane); break;
           }
         } else {
           if (width == 32)
-            epi_pass<32, false>(p, &map_h, taddr, c0, row, row0, box, s_att, att, ps, pd, cur, lane);
+            epi_pass<32, false>(p, &map_h, taddr, c0, row, row0, box, s_att, att, ps, pd, cur, head_end, lane);
           else
-            epi_pass<16, false>(p, &map_h, taddr, c0, row, row0, box, s_att, att, ps, pd, cur, lane);
+            epi_pass<16, false>(p, &map_h, taddr, c0, row, row0, box, s_att, att, ps, pd, cur, head_end, lane);
         }
       }
-      if (att && cur >= 0) att_flush(p, row, cur, ps, pd);
+      if (att && c_begin < c_end) att_flush(p, row, cur, ps, pd);
       // Accumulator fully read: hand it back to the MMA warp.
       tc_fence_before();
       __syncwarp();
