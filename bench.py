@@ -228,18 +228,24 @@ def broadcast_workload(rank, world, device, scale=1.0):
 
 class NeededExchange:
     """Layer on `world` ranks moving only the remote input rows this rank's
-    edges read (partition.NeededRows): each owner packs, per requester, the
-    rows it needs into one block of its exported pack buffer (gnnc_gather_rows);
-    each requester pulls one block per owner with the copy engines into its
-    compact table, pipelined with the projection; the local CSR's columns are
-    relabelled to compact-table rows. Three one-word NCCL all-reduces per step
-    order the owners' input writes, their packs and the peers' reads."""
+    edges read (partition.NeededRows); the local CSR's columns are relabelled
+    to compact-table rows. Two ways to move them:
+
+    * read="copy": each owner packs, per requester, the rows it needs into one
+      block of its exported pack buffer (gnnc_gather_rows); each requester
+      pulls one block per owner with the copy engines into its compact table,
+      pipelined with the projection. Three one-word NCCL all-reduces per step
+      order the owners' input writes, their packs and the peers' reads.
+    * read="gather": each requester gathers the rows straight from the owners'
+      mapped input blocks (gnnc_gather_rows with plain loads over NVLink: no
+      pack, no third fence), then projects its own and the gathered rows."""
 
     PIECE_ROWS = 1 << 18
 
-    def __init__(self, P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device):
+    def __init__(self, P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device,
+                 read="copy"):
         N = x_d.size(0)
-        self.P, self.rt, self.N = P, rt, N
+        self.P, self.rt, self.N, self.read = P, rt, N, read
         self.rr = rr = P.row_range(N, world, rank)
         rowptr_l, col_l = P.local_csr(rowptr, col, rr)
         self.need = need = P.NeededRows(col_l, rr)
@@ -249,8 +255,13 @@ class NeededExchange:
         R = rr.rows_per_rank
         self.x_own = torch.zeros((R, ld), dtype=torch.bfloat16, device=device)
         self.x_own[: rr.count, :IN] = x_d[rr.begin : rr.end]
-        self.pack = torch.zeros((max(1, need.pack_rows), ld), dtype=torch.bfloat16, device=device)
-        self.peers = P.PeerBuffers(self.pack)
+        if read == "gather":
+            self.pack = None
+            self.peers = P.PeerRows(self.x_own, rr, N)
+        else:
+            self.pack = torch.zeros((max(1, need.pack_rows), ld), dtype=torch.bfloat16,
+                                    device=device)
+            self.peers = P.PeerBuffers(self.pack)
         nc = need.compact_rows
         self.xc = torch.zeros((max(1, nc - R), ld), dtype=torch.bfloat16, device=device)
         self.h_full = rt.empty_rows(nc, F, torch.bfloat16, device)
@@ -267,11 +278,20 @@ class NeededExchange:
                 self.pieces.append((p, a, min(n_p, a + self.PIECE_ROWS)))
         self.side = torch.cuda.Stream(device)
         self.piece_ev = [torch.cuda.Event() for _ in self.pieces]
-        self.proj_launches = 1 + len(self.pieces) + 1  # projections + the pack
         remote = max(1, N - rr.count)
-        self.describe = (f"owners pack, requesters pull only the remote input rows their edges "
-                         f"read ({sum(need.need_rows) / remote:.0%} of the remote rows here) over "
-                         "NVLink with the copy engines (CUDA IPC), pipelined with the projection")
+        share = f"{sum(need.need_rows) / remote:.0%} of the remote rows here"
+        if read == "gather":
+            self.order = P.read_order(rr)[1:]
+            n_gathers = sum(1 for p in self.order if need.need_rows[p])
+            self.proj_launches = n_gathers + 2  # gathers + own and remote projections
+            self.describe = (f"requesters gather only the remote input rows their edges read "
+                             f"({share}) from the owners' mapped blocks with plain loads over "
+                             "NVLink (CUDA IPC), then project own and gathered rows")
+        else:
+            self.proj_launches = 1 + len(self.pieces) + 1  # projections + the pack
+            self.describe = (f"owners pack, requesters pull only the remote input rows their "
+                             f"edges read ({share}) over NVLink with the copy engines (CUDA IPC), "
+                             "pipelined with the projection")
 
     def x_local_rows(self):
         return self.x_own[: self.n_loc, :IN]
@@ -288,6 +308,8 @@ class NeededExchange:
                      adst_out=adst)
 
     def project(self):
+        if self.read == "gather":
+            return self._project_gather()
         need, rt, R = self.need, self.rt, self.rr.rows_per_rank
         self.fence()  # every rank's input rows are written
         if need.pack_rows:
@@ -311,6 +333,20 @@ class NeededExchange:
             # a_dst of remote rows is not used: it goes to a scratch buffer
             self._proj(xs, slice(lo, lo + (b - a)), self._dscratch(b - a))
         self.fence()  # every rank is done reading the packs
+
+    def _project_gather(self):
+        need, rt, R = self.need, self.rt, self.rr.rows_per_rank
+        self.fence()  # every rank's input rows are written
+        for p in self.order:  # rotated: each owner serves one requester at a time
+            if need.need_rows[p]:
+                lo = need.base[p] - R
+                rt.gather_rows(self.peers.view(p, IN), need.need_idx[p], self.xc[lo:])
+        self.fence()  # every rank is done reading the owners' blocks
+        n = self.n_loc
+        self._proj(self.x_own[:n, :IN], slice(0, n), self.d_own[:n])
+        nr = need.compact_rows - R
+        if nr:
+            self._proj(self.xc[:nr, :IN], slice(R, R + nr), self._dscratch(nr))
 
     def _dscratch(self, rows):
         if getattr(self, "_ds", None) is None or self._ds.size(0) < rows:
@@ -531,7 +567,8 @@ def run_b200(args) -> None:
     bias = conv.bias.detach().to(device)
     chunks = args.chunks or (1 if world == 1 else 4)
     if args.exchange == "needed" and world > 1:
-        lay = NeededExchange(P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device)
+        lay = NeededExchange(P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device,
+                             read="gather" if args.peer_read == "gather" else "copy")
     elif args.exchange == "peer" and world > 1:
         if args.piece_rows:
             PeerExchange.PIECE_ROWS = args.piece_rows
@@ -1051,8 +1088,10 @@ def main() -> None:
                          "all-gather the input X, or all-gather the projected h")
     ap.add_argument("--piece-rows", type=int, default=0,
                     help="peer exchange: rows per pulled piece (default 2^18)")
-    ap.add_argument("--peer-read", default="copy", choices=("copy", "tma"),
-                    help="peer exchange: copy-engine staging (default) or direct TMA reads")
+    ap.add_argument("--peer-read", default="copy", choices=("copy", "tma", "gather"),
+                    help="peer exchange: copy-engine staging (default) or direct TMA reads; "
+                         "needed exchange: owner packs + copy-engine pulls (copy, default) or "
+                         "requester-side gathers over NVLink (gather)")
     ap.add_argument("--chunks", type=int, default=0,
                     help="input exchange: all-gather pieces (default 1 on one GPU, else 4)")
     ap.add_argument("--e2e-steps", type=int, default=30)
@@ -1066,6 +1105,10 @@ def main() -> None:
     ap.add_argument("--scale", type=float, default=1.0,
                     help="shrink the graph (profiling captures only; not a bench line)")
     args = ap.parse_args()
+    if args.peer_read == "gather" and args.exchange != "needed":
+        ap.error("--peer-read gather goes with --exchange needed")
+    if args.peer_read == "tma" and args.exchange != "peer":
+        ap.error("--peer-read tma goes with --exchange peer")
     if args.warmup < 3 and args.impl == "b200":
         log("[bench] warmup raised to 3 (minimum)")
         args.warmup = 3

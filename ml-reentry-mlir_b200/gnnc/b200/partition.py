@@ -286,6 +286,9 @@ class NeededRows:
     * as requester, a rank lands owner p's block at rows `base[p]` of its
       compact table, whose first R rows are its own;
     * `col` is the local CSR's column array relabelled to compact-table rows.
+
+    `need_idx[p]` keeps the requester's list for owner p on the device, for a
+    requester that gathers the rows itself from p's mapped block (no pack).
     """
 
     def __init__(self, col_l: torch.Tensor, rr: RowRange, group=None) -> None:
@@ -310,6 +313,7 @@ class NeededRows:
         dist.all_gather_object(offs, self.pack_off, group=group)
         self.remote_off = [offs[p][me] for p in range(W)]  # my block in p's pack buffer
         self.need_rows = [int(t.numel()) for t in need]
+        self.need_idx = [t.to(dev) for t in need]
         self.base = [0] * W
         nxt = R
         for p in read_order(rr)[1:]:

@@ -616,21 +616,31 @@ def peer_copy(dst: torch.Tensor | DeviceRows, src: torch.Tensor | DeviceRows, nb
     Context.get(dev).call("gnnc_peer_copy", ptr["dst"], ptr["src"], nbytes)
 
 
-def gather_rows(src: torch.Tensor, idx: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
-    """out[i] = src[idx[i]] (whole padded rows; 16-byte aligned row strides)."""
-    _check_cuda(src, idx, out)
+def gather_rows(src: torch.Tensor | DeviceRows, idx: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out[i] = src[idx[i]] (whole padded rows; 16-byte aligned row strides).
+
+    src may be a DeviceRows, e.g. another process's rows mapped by peer_open:
+    the kernel then reads them over NVLink with plain loads."""
+    if isinstance(src, DeviceRows):
+        _check_cuda(idx, out)
+        if src.device != out.device:
+            raise ValueError("src rows must be addressable on out's device")
+        esz = torch.empty((), dtype=src.dtype).element_size()
+        src_ptr, src_ld, n_src, dtype = src.ptr, src.ld, src.rows, src.dtype
+    else:
+        _check_cuda(src, idx, out)
+        esz = src.element_size()
+        src_ptr, src_ld, n_src, dtype = src.data_ptr(), src.stride(0), src.size(0), src.dtype
     if idx.dtype != torch.int32 or not idx.is_contiguous():
         raise ValueError("idx must be a contiguous int32 tensor")
     n = idx.numel()
-    if out.size(0) < n or out.dtype != src.dtype:
+    if out.size(0) < n or out.dtype != dtype:
         raise ValueError("out must hold len(idx) rows of src's dtype")
-    esz = src.element_size()
-    row_bytes = src.stride(0) * esz
+    row_bytes = src_ld * esz
     if out.stride(0) * esz < row_bytes:
         raise ValueError("out rows are narrower than src rows")
-    Context.get(src.device).call("gnnc_gather_rows", src.data_ptr(), src.stride(0) * esz,
-                                 idx.data_ptr(), n, src.size(0), out.data_ptr(),
-                                 out.stride(0) * esz, row_bytes)
+    Context.get(out.device).call("gnnc_gather_rows", src_ptr, row_bytes, idx.data_ptr(), n, n_src,
+                                 out.data_ptr(), out.stride(0) * esz, row_bytes)
     return out
 
 

@@ -205,8 +205,18 @@ def _rank_needed(rank, world, port, out_dir):
             off = plan.remote_off[p]
             table[plan.base[p] : plan.base[p] + plan.need_rows[p]] = blocks[p][off : off + plan.need_rows[p]]
     ok = torch.equal(table[plan.col.long()], x[col_l.long()])
+    # requester-side gathers: rows need_idx[p] of owner p's block land at base[p]
+    owners: list = [None] * world
+    dist.all_gather_object(owners, x_own)  # stands in for the mapped blocks
+    table2 = torch.zeros_like(table)
+    table2[:R] = x_own
+    for p in range(world):
+        if p != rank and plan.need_rows[p]:
+            table2[plan.base[p] : plan.base[p] + plan.need_rows[p]] = owners[p][plan.need_idx[p].long()]
+    ok_gather = torch.equal(table2, table)
     frac = sum(plan.need_rows) / max(1, n - rr.count)
-    torch.save({"ok": ok, "frac": frac}, os.path.join(out_dir, f"n{rank}.pt"))
+    torch.save({"ok": ok, "ok_gather": ok_gather, "frac": frac},
+               os.path.join(out_dir, f"n{rank}.pt"))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -215,12 +225,13 @@ def _rank_needed(rank, world, port, out_dir):
 def test_needed_rows_relabel_and_offsets_gloo(tmp_path):
     """Three ranks: each packs the rows the others need, the blocks travel
     (all_gather here, peer pulls on the GPU), and the compact table indexed by
-    the relabelled columns gives every edge its source row."""
+    the relabelled columns gives every edge its source row; the requester-side
+    gathers (need_idx per owner) build the same table."""
     import torch.multiprocessing as mp
 
     world = 3
     mp.spawn(_rank_needed, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
     for r in range(world):
         got = torch.load(tmp_path / f"n{r}.pt")
-        assert got["ok"]
+        assert got["ok"] and got["ok_gather"]
         assert 0.0 < got["frac"] <= 1.0
