@@ -148,7 +148,10 @@ GNNC_API int gnnc_csr_validate(gnnc_ctx_t* ctx, const int32_t* rowptr, const int
  * split_threshold are cut into segments of at most split_threshold edges
  * processed by separate CTAs and combined by a merge step. The plan depends
  * only on rowptr (device, n_rows+1 entries) and is reused across layers and
- * calls. 0 selects the defaults (cta_threshold 256, split_threshold 4096).
+ * calls. 0 selects the defaults: cta_threshold 256 (launches on 256-wide
+ * rows give rows of up to 1024 edges to the warp path), split_threshold
+ * max(4096, edges / (2 * SMs * 4)), so a row is split only when it is a
+ * sizeable share of the launch. Replaces the survey's gnnc_row_split_plan.
  * Synchronous (reads rowptr back once). */
 GNNC_API int gnnc_plan_create(gnnc_ctx_t* ctx, const int32_t* rowptr, int64_t n_rows,
                      int32_t cta_threshold, int32_t split_threshold, gnnc_plan_t** out_plan);
@@ -302,6 +305,28 @@ GNNC_API int gnnc_peer_close(gnnc_ctx_t* ctx, void* ptr, uint64_t offset);
 GNNC_API int gnnc_gather_rows(gnnc_ctx_t* ctx, const void* src, int64_t ld_src,
                               const int32_t* idx, int64_t n, int64_t n_src, void* dst,
                               int64_t ld_dst, int64_t row_bytes);
+
+/* One NCCL communicator per context, for the exchange step of a
+ * destination-row partition (replaces the reference-side all-gather a
+ * partitioned layer needs; the reference itself has no multi-GPU path,
+ * internal-docs/project-summary.md:105):
+ *   gnnc_comm_unique_id : rank 0 makes the id (GNNC_COMM_ID_BYTES bytes) and
+ *                         hands it to the other ranks by any host means
+ *   gnnc_comm_init      : joins communicator `id` as `rank` of `nranks` on
+ *                         ctx's device (blocks until every rank has joined)
+ *   gnnc_allgather      : recvbuf[r*count .. (r+1)*count) = rank r's sendbuf
+ *                         (count elements of dtype GNNC_F32 or GNNC_BF16), on
+ *                         ctx's stream
+ *   gnnc_comm_destroy   : waits for ctx's stream, destroys the communicator
+ *                         (gnnc_destroy also does)
+ * NCCL is loaded on first use (the copy already in the process, else
+ * libnccl.so.2); failures return GNNC_ERR_NCCL with NCCL's message. */
+#define GNNC_COMM_ID_BYTES 128
+GNNC_API int gnnc_comm_unique_id(gnnc_ctx_t* ctx, void* id);
+GNNC_API int gnnc_comm_init(gnnc_ctx_t* ctx, const void* id, int rank, int nranks);
+GNNC_API int gnnc_allgather(gnnc_ctx_t* ctx, const void* sendbuf, void* recvbuf, size_t count,
+                            int dtype);
+GNNC_API int gnnc_comm_destroy(gnnc_ctx_t* ctx);
 
 #ifdef __cplusplus
 }

@@ -81,7 +81,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
         objs = list(pool.map(compile_one, sources))
     if force or _stale(LIB, objs):
         tmp = LIB.with_suffix(".so.tmp")
-        cmd = [exe, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-cudart", "static"]
+        cmd = [exe, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-cudart", "static", "-ldl"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"link failed:\n{res.stdout}{res.stderr}")

@@ -23,6 +23,10 @@ struct gnnc_ctx {
   bool ws_owned = true;
   // Small device area: [0..7] scheduling counters, [8..15] result/error words.
   int* dev_words = nullptr;
+  // NCCL communicator (ncclComm_t) of gnnc_comm_init, or null.
+  void* comm = nullptr;
+  int comm_rank = 0;
+  int comm_size = 1;
 };
 
 // Row schedule for one CSR (see gnnc_plan_create in gnnc_b200.h).
@@ -54,6 +58,9 @@ struct gnnc_plan {
 namespace gnnc {
 
 int set_error(gnnc_ctx_t* ctx, int status, const char* fmt, ...);
+
+// Destroys the context's communicator, if any (comm.cu).
+void comm_release(gnnc_ctx_t* ctx);
 
 // Returns GNNC_ERR_CUDA with text if err != cudaSuccess.
 int cuda_status(gnnc_ctx_t* ctx, cudaError_t err, const char* what);

@@ -88,6 +88,7 @@ int gnnc_destroy(gnnc_ctx_t* ctx) {
   if (!ctx) return GNNC_OK;
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
+  gnnc::comm_release(ctx);
   if (ctx->ws && ctx->ws_owned) cudaFree(ctx->ws);
   if (ctx->dev_words) cudaFree(ctx->dev_words);
   delete ctx;

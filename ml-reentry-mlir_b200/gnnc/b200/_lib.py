@@ -80,6 +80,10 @@ SIGNATURES: dict[str, tuple] = {
     "gnnc_peer_close": (c_int, [_P, _P, ctypes.c_uint64]),
     "gnnc_peer_copy": (c_int, [_P, _P, _P, c_size_t]),
     "gnnc_gather_rows": (c_int, [_P, _P, _I64, _P, _I64, _I64, _P, _I64, _I64]),
+    "gnnc_comm_unique_id": (c_int, [_P, _P]),
+    "gnnc_comm_init": (c_int, [_P, _P, c_int, c_int]),
+    "gnnc_allgather": (c_int, [_P, _P, _P, c_size_t, c_int]),
+    "gnnc_comm_destroy": (c_int, [_P]),
     "gnnc_gat_aggregate_noalloc": (
         c_int,
         [

@@ -644,6 +644,43 @@ def gather_rows(src: torch.Tensor | DeviceRows, idx: torch.Tensor, out: torch.Te
     return out
 
 
+COMM_ID_BYTES = 128
+
+
+def comm_unique_id(device: torch.device | int) -> bytes:
+    """A new NCCL communicator id (rank 0 makes it; the ranks share it on the host)."""
+    ctx = Context.get(device)
+    uid = ctypes.create_string_buffer(COMM_ID_BYTES)
+    raise_for(ctx.lib.gnnc_comm_unique_id(ctx.handle, uid), ctx.handle, "gnnc_comm_unique_id")
+    return uid.raw
+
+
+def comm_init(device: torch.device | int, uid: bytes, rank: int, nranks: int) -> None:
+    """Joins communicator `uid` as `rank` of `nranks` (blocks until all have joined)."""
+    if len(uid) != COMM_ID_BYTES:
+        raise ValueError(f"communicator id must be {COMM_ID_BYTES} bytes")
+    ctx = Context.get(device)
+    raise_for(ctx.lib.gnnc_comm_init(ctx.handle, uid, rank, nranks), ctx.handle, "gnnc_comm_init")
+
+
+def allgather(send: torch.Tensor, recv: torch.Tensor) -> torch.Tensor:
+    """recv = every rank's `send`, concatenated in rank order, on the context's stream."""
+    _check_cuda(send, recv)
+    if not (send.is_contiguous() and recv.is_contiguous()) or send.dtype != recv.dtype:
+        raise ValueError("send and recv must be contiguous tensors of one dtype")
+    ctx = Context.get(send.device)
+    if recv.numel() % max(1, send.numel()) != 0:
+        raise ValueError("recv must hold a whole number of send buffers")
+    raise_for(ctx.lib.gnnc_allgather(ctx.handle, send.data_ptr(), recv.data_ptr(), send.numel(),
+                                     _dt(send)), ctx.handle, "gnnc_allgather")
+    return recv
+
+
+def comm_destroy(device: torch.device | int) -> None:
+    ctx = Context.get(device)
+    raise_for(ctx.lib.gnnc_comm_destroy(ctx.handle), ctx.handle, "gnnc_comm_destroy")
+
+
 def peer_close(device: torch.device | int, ptr: int, offset: int) -> None:
     ctx = Context.get(device)
     raise_for(ctx.lib.gnnc_peer_close(ctx.handle, ptr, offset), ctx.handle, "gnnc_peer_close")

@@ -56,6 +56,10 @@ def test_null_arguments_are_rejected_without_a_device():
     assert lib.gnnc_synchronize(None) == _lib.ERR_INVALID
     assert lib.gnnc_plan_info(None, None) == _lib.ERR_INVALID
     assert lib.gnnc_destroy(None) == _lib.OK
+    assert lib.gnnc_comm_unique_id(None, None) == _lib.ERR_INVALID
+    assert lib.gnnc_comm_init(None, None, 0, 1) == _lib.ERR_INVALID
+    assert lib.gnnc_allgather(None, None, None, 0, 0) == _lib.ERR_INVALID
+    assert lib.gnnc_comm_destroy(None) == _lib.ERR_INVALID
     assert lib.gnnc_plan_destroy(None) == _lib.OK
 
 
