@@ -3,8 +3,9 @@
 A second process maps the first process's input block (CUDA IPC; both on
 cuda:0, so the test needs one GPU) and runs the projection with its x operand
 read through the mapping; the result must equal the projection of the same
-rows read locally, bit for bit (same kernel, same operands). This is the read
-path the multi-GPU layer uses for remote input rows."""
+rows read locally, bit for bit (same kernel, same operands), and rows gathered
+from the mapping (gnnc_gather_rows) equal the same rows of the block. These
+are the read paths the multi-GPU layer uses for remote input rows."""
 
 from __future__ import annotations
 
@@ -43,8 +44,13 @@ def _child(handle, offset, rows, cols, ld, dtype_name, out_path):
                             out_dtype=torch.bfloat16)
     # a row slice of the mapping reads the right rows
     h2 = rt.proj(xv[rows // 3 : rows // 3 + 100], W.to(dev), out_dtype=torch.bfloat16)
+    # whole padded rows gathered straight from the mapping (plain loads)
+    idx = torch.randint(0, rows, (999,), generator=torch.Generator().manual_seed(9),
+                        dtype=torch.int32).to(dev)
+    g = rt.gather_rows(xv, idx, torch.zeros((999, ld), dtype=dtype, device=dev))
     rt.Context.get(dev).synchronize()
-    torch.save({"h": h.cpu(), "asrc": asrc.cpu(), "adst": adst.cpu(), "h2": h2.cpu()}, out_path)
+    torch.save({"h": h.cpu(), "asrc": asrc.cpu(), "adst": adst.cpu(), "h2": h2.cpu(),
+                "g": g.cpu(), "idx": idx.cpu()}, out_path)
     rt.peer_close(dev, ptr, offset)
 
 
@@ -80,6 +86,8 @@ def test_projection_reads_a_peer_mapped_buffer(device, tmp_path, dtype):
     assert torch.equal(got["asrc"], asrc.cpu())
     assert torch.equal(got["adst"], adst.cpu())
     assert torch.equal(got["h2"], h2.cpu())
+    bits = torch.int16 if dtype == torch.bfloat16 else torch.int32
+    assert torch.equal(got["g"].view(bits), block.view(bits)[got["idx"].long()])
 
 
 def test_peer_export_rejects_host_memory(device):
