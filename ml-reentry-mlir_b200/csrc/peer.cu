@@ -34,24 +34,34 @@ GetAddressRangeFn range_fn(gnnc_ctx_t* ctx) {
   return g_range;
 }
 
-// One warp per destination row: dst[i] = src[idx[i]] (row_bytes bytes, 16-byte
-// chunks). An index outside [0, n_src) leaves the row alone and raises the
-// context's bad-index word (reported by gnnc_synchronize).
+// dst[i] = src[idx[i]] for rows of `chunks` 16-byte chunks. A warp copies
+// 32 / chunks rows per pass when a row has fewer than 32 chunks (lane ->
+// (row slot, chunk), e.g. two 13-chunk rows of 100 bf16 features, 26 lanes
+// busy), else one row with its lanes striding over the chunks. An index
+// outside [0, n_src) leaves the row alone and raises the context's bad-index
+// word (reported by gnnc_synchronize). No lane waits on another.
 __global__ void gather_rows_kernel(const char* __restrict__ src, int64_t ld_src,
                                    const int32_t* __restrict__ idx, int64_t n, int64_t n_src,
                                    char* __restrict__ dst, int64_t ld_dst, int64_t chunks,
                                    int* bad) {
   const int lane = threadIdx.x & 31;
+  const bool packed = chunks < 32;
+  const int rpw = packed ? int(32 / chunks) : 1;
+  const int slot = packed ? lane / int(chunks) : 0;
+  const int c0 = packed ? lane - slot * int(chunks) : lane;
+  const int64_t step = packed ? chunks : 32;
+  if (slot >= rpw) return;  // the few lanes past the last whole row
   const int64_t warps = int64_t(gridDim.x) * (blockDim.x / 32);
-  for (int64_t i = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) / 32; i < n; i += warps) {
+  const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
+  for (int64_t i = warp * rpw + slot; i < n; i += warps * rpw) {
     const int32_t r = __ldg(idx + i);
     if (r < 0 || r >= n_src) {
-      if (lane == 0) atomicOr(bad, 1);
+      if (c0 == 0) atomicOr(bad, 1);
       continue;
     }
     const uint4* s = reinterpret_cast<const uint4*>(src + int64_t(r) * ld_src);
     uint4* d = reinterpret_cast<uint4*>(dst + i * ld_dst);
-    for (int64_t c = lane; c < chunks; c += 32) d[c] = __ldg(s + c);
+    for (int64_t c = c0; c < chunks; c += step) d[c] = __ldg(s + c);
   }
 }
 
@@ -71,12 +81,14 @@ int gnnc_gather_rows(gnnc_ctx_t* ctx, const void* src, int64_t ld_src, const int
   GNNC_CHECK_ARG(ctx, ld_src >= row_bytes && ld_dst >= row_bytes, "stride below row size");
   if (n == 0) return GNNC_OK;
   GNNC_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
-  const int64_t want = (n + 7) / 8;
+  const int64_t chunks = row_bytes / 16;
+  const int64_t rows_per_cta = 8 * (chunks < 32 ? 32 / chunks : 1);  // 8 warps
+  const int64_t want = (n + rows_per_cta - 1) / rows_per_cta;
   const int64_t cap = int64_t(ctx->num_sms) * 8;
   const unsigned grid = unsigned(want < cap ? want : cap);
   gather_rows_kernel<<<grid, 256, 0, ctx->stream>>>(
       static_cast<const char*>(src), ld_src, idx, n, n_src, static_cast<char*>(dst), ld_dst,
-      row_bytes / 16, ctx->dev_words + 2);
+      chunks, ctx->dev_words + 2);
   GNNC_CUDA_TRY(ctx, cudaGetLastError());
   return GNNC_OK;
 }
