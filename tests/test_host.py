@@ -2,6 +2,8 @@
 
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -162,3 +164,17 @@ def test_graph_cache_key_survives_detach_and_tracks_updates():
     assert B200Executable._graph_key(ei.detach()) != k1
     other = ei.clone()
     assert B200Executable._graph_key(other) != B200Executable._graph_key(ei)
+
+
+def test_bench_rejects_read_modes_of_another_exchange():
+    """bench.py: --peer-read gather belongs to the needed-rows exchange and tma
+    to the peer exchange; other pairings stop at argument parsing."""
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for args, msg in ((["--peer-read", "gather"], "goes with --exchange needed"),
+                      (["--exchange", "needed", "--peer-read", "tma"], "goes with --exchange peer")):
+        res = subprocess.run([sys.executable, os.path.join(root, "bench.py"), *args],
+                             capture_output=True, text=True, timeout=300)
+        assert res.returncode == 2 and msg in res.stderr, res.stderr[-500:]
