@@ -11,12 +11,16 @@ for ogbn-products (no dataset content is available or used).
 One step = the whole layer: the projection (gnnc_proj: h = X W^T with the
 attention coefficients a_src, a_dst in its epilogue) and the fused aggregation
 (gnnc_gat_aggregate: SDDMM, LeakyReLU, edge softmax, SpMM, bias, ELU). With
---gpus N (one process per GPU under torchrun) each rank owns a block-cyclic
-set of destination rows and their input features; the 100-wide input rows are
-all-gathered over NCCL in pieces (208 bytes a row instead of the 528 of h and
-a_src) on a side stream while the projection of the pieces already received
-runs, every rank projects all rows, and each rank aggregates its own rows
-(--exchange output: project own rows, all-gather h and a_src instead).
+--gpus N (one process per GPU under torchrun) each rank owns a contiguous
+range of destination rows and their input features; the 100-wide input rows
+cross NVLink (208 bytes a row instead of the 528 of h and a_src): the copy
+engines pull the other ranks' rows from their HBM (CUDA IPC mappings) in
+pieces on a side stream while the projection of the pieces already present
+runs, every rank projects all rows, and each rank aggregates its own rows with
+the single-GPU plan's split decisions (rows identical to one GPU's, checked by
+--check). --exchange selects the alternatives: needed (only the remote rows a
+rank's edges read), input (NCCL all-gather of X), output (project own rows,
+all-gather h and a_src).
 
 Printed (rank 0, one JSON line): value = stored edges x steps / device time
 (max over ranks); e2e = the same metric through gnnc.execution.run_jit with
@@ -579,10 +583,15 @@ def run_b200(args) -> None:
     else:
         lay = OutputExchange(P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device)
     full = (rowptr, col, x_d) if args.check else None
+    split = args.split_threshold
+    if world > 1 and split == 0:
+        # split the rows the single-GPU plan splits: bit-identical rows at every N
+        sms = torch.cuda.get_device_properties(device).multi_processor_count
+        split = P.whole_graph_split_threshold(col.numel(), sms)
     del rowptr, col, x_d
     rowptr_l, col_l = lay.rowptr_l, lay.col_l
     n_loc, e_loc = lay.n_loc, col_l.numel()
-    plan = rt.Plan(rowptr_l, cta_threshold=args.cta_threshold, split_threshold=args.split_threshold)
+    plan = rt.Plan(rowptr_l, cta_threshold=args.cta_threshold, split_threshold=split)
     info = plan.info()
     out_l = rt.empty_rows(n_loc, F, torch.bfloat16, device)
     project = lay.project
@@ -643,6 +652,11 @@ def run_b200(args) -> None:
         check = check_rows(rt, lay, full, W, att_s, att_d, bias, out_l, device)
         log(f"[bench] rank {rank}: own rows vs the single-GPU layer: {check}")
         full = None
+        if world > 1:  # the line reports every rank's verdict
+            verdicts: list = [None] * world
+            dist.all_gather_object(verdicts, check)
+            bad = [r for r, v in enumerate(verdicts) if v != "bit-exact"]
+            check = "bit-exact" if not bad else f"MISMATCH on ranks {bad}"
 
     # ---- end to end through the public API (host buffers, copies timed) ----
     e2e = None

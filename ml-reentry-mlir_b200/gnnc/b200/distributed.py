@@ -158,7 +158,10 @@ class DistributedExecutable:
             parts = P.local_csr(g.rowptr, g.col, rr, extra)
             rowptr_l, col_l = parts[0], parts[1]
             w_l = parts[2] if g.w is not None else None
-            plan = rt.Plan(rowptr_l)
+            # the single-GPU plan's split decisions (bit-identical rows)
+            sms = torch.cuda.get_device_properties(dev).multi_processor_count
+            plan = rt.Plan(rowptr_l, split_threshold=P.whole_graph_split_threshold(
+                g.col.numel(), sms))
             ld_in = rt.row_stride(layer.in_channels, dt)
             ld_f = rt.row_stride(layer.width, dt)
             gat = layer.kind == "gat"

@@ -74,6 +74,19 @@ def local_csr(rowptr: torch.Tensor, col: torch.Tensor, rr: RowRange, extra: tupl
     return tuple(out)
 
 
+def whole_graph_split_threshold(total_edges: int, num_sms: int) -> int:
+    """The split threshold gnnc_plan_create picks by default for a CSR of
+    `total_edges` edges on a GPU of `num_sms` SMs: max(4096, edges / (2 * SMs * 4)).
+
+    A rank's plan covers only its rows, so its own default would follow its
+    smaller edge count and split rows the single-GPU plan keeps whole (a split
+    row sums its edges in segments: the same value up to rounding). Giving each
+    rank this threshold makes it split exactly the rows one GPU would, so the
+    partitioned results equal the single-GPU results bit for bit."""
+    per = int(total_edges) // (2 * int(num_sms) * 4)
+    return int(min(max(4096, per), 1 << 30))
+
+
 def gathered_table(rr: RowRange, width: int, dtype: torch.dtype, device) -> torch.Tensor:
     """[world*R, width] all-gather buffer; rank r's slot is rows [r*R, r*R + R)."""
     return torch.empty((rr.world * rr.rows_per_rank, width), dtype=dtype, device=device)

@@ -341,3 +341,40 @@ def test_sage_aggregate_matches_oracle(device, F, dtype, act, lsm, cta, split):
     if lsm:
         ref = torch.log_softmax(ref, dim=-1)
     assert_close(out, ref)
+
+
+def test_partition_plans_split_like_the_whole_graph(device):
+    """A rank's plan given whole_graph_split_threshold splits exactly the rows
+    the single-GPU plan splits, so its output rows equal the single-GPU rows
+    bit for bit (its own default follows its smaller edge count and may split
+    rows the single-GPU plan keeps whole)."""
+    from gnnc.b200 import partition as P
+    from gnnc.b200 import runtime as rt
+
+    g = torch.Generator().manual_seed(11)
+    n = 100_000
+    deg = torch.randint(20, 80, (n,), generator=g)
+    hubs = torch.randperm(n, generator=g)[:40]
+    deg[hubs] = torch.randint(4200, 9000, (40,), generator=g)  # between the two thresholds
+    rowptr = torch.zeros(n + 1, dtype=torch.int64)
+    rowptr[1:] = deg.cumsum(0)
+    E = int(rowptr[-1])
+    col = torch.randint(0, n, (E,), generator=g, dtype=torch.int32)
+    rowptr_d, col_d = rowptr.to(torch.int32).to(device), col.to(device)
+    h = torch.randn(n, 256, generator=g).to(torch.bfloat16).to(device)
+    a = (torch.randn(n, 4, generator=g) * 0.5).to(device)
+    d = (torch.randn(n, 4, generator=g) * 0.5).to(device)
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    thr = P.whole_graph_split_threshold(E, sms)
+    assert thr > 4096  # the graph is large enough for the adaptive default
+    whole = rt.Plan(rowptr_d)
+    assert whole.info() == rt.Plan(rowptr_d, split_threshold=thr).info()
+    kw = dict(heads=4, concat=True, act=rt.ACT_ELU, out_dtype=torch.bfloat16)
+    full = rt.gat_aggregate(whole, rowptr_d, col_d, h, a, d, **kw)
+    for r in range(4):
+        rr = P.row_range(n, 4, r)
+        rp_l, col_l = P.local_csr(rowptr_d, col_d, rr)
+        plan = rt.Plan(rp_l, split_threshold=thr)
+        assert plan.info()["n_split_rows"] == int((deg[rr.begin : rr.end] > thr).sum())
+        out = rt.gat_aggregate(plan, rp_l, col_l, h, a, d[rr.begin : rr.end], **kw)
+        assert torch.equal(out, full[rr.begin : rr.end]), f"rank {r}"

@@ -235,3 +235,12 @@ def test_needed_rows_relabel_and_offsets_gloo(tmp_path):
         got = torch.load(tmp_path / f"n{r}.pt")
         assert got["ok"] and got["ok_gather"]
         assert 0.0 < got["frac"] <= 1.0
+
+
+def test_whole_graph_split_threshold_formula():
+    """gnnc_plan_create's default: max(4096, edges / (2 * SMs * 4)), capped at 2^30."""
+    from gnnc.b200 import partition as P
+
+    assert P.whole_graph_split_threshold(64_308_169, 148) == 64_308_169 // 1184
+    assert P.whole_graph_split_threshold(1000, 148) == 4096
+    assert P.whole_graph_split_threshold(1 << 45, 148) == 1 << 30
