@@ -117,11 +117,11 @@ struct VecLoad<__nv_bfloat16, 1> {
   }
 };
 
-// ELU as exp(x) - 1 for x <= 0 with the fast exponential (absolute error
-// ~1e-7 on [-inf, 0], far inside the fp32 parity tolerance).
+// ELU as expm1(x) for x <= 0, as torch's elu computes it: forming exp(x) - 1
+// would cancel for small |x| and lose the relative accuracy there.
 __device__ __forceinline__ float apply_act(float v, int act) {
   if (act == GNNC_ACT_RELU) return fmaxf(v, 0.f);
-  if (act == GNNC_ACT_ELU) return v > 0.f ? v : __expf(v) - 1.f;
+  if (act == GNNC_ACT_ELU) return v > 0.f ? v : expm1f(v);
   return v;
 }
 

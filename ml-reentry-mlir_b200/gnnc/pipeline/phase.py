@@ -1,26 +1,37 @@
-"""Phases group compile steps so a caller can stop, print or trace at a boundary.
+"""Named compile phases: a caller can halt, dump or trace at any phase boundary.
 
-Same surface as the reference's gnnc/pipeline/phase.py:50-246 (PhasePipeline,
-CallablePhase, PhaseNotReached; add_callable_phase, extend, names, find, run
-with stop_before / stop_after / print_ir_before / print_ir_after / emit), so
-`--trace` and `--stop-*` keep working for the B200 target. The MLIR-only
-StagePhase (a lazily built Lighthouse PipelineDriver) has no counterpart: the
-B200 phases are Python callables over an fx graph and a kernel program.
+Public surface kept from the reference's gnnc/pipeline/phase.py:50-246 so that
+`gnnc-bench --trace`, `--stop-before/--stop-after` and `--print-ir-*` behave the
+same for the B200 target: `PhasePipeline` (`add_callable_phase`, `extend`,
+`names`, `find`, `run`), `CallablePhase`, `PhaseNotReached`, and `run`'s
+keyword arguments and `(module, [(phase, passes), ...])` result. The
+reference's MLIR-only StagePhase (a Lighthouse pass driver) has no counterpart:
+every B200 phase is a Python callable over an fx graph or a kernel program.
+
+Implementation. A pipeline keeps its phases in order plus a name -> position
+map. `run` first turns its arguments into a `_Schedule` (how many phases run,
+and for each of them whether to dump the module before / after it), checking
+every named phase against the position map in one pass, and only then folds
+the module through the scheduled phases. Nothing runs if any argument is bad.
 """
 
 from __future__ import annotations
 
 from abc import ABC, abstractmethod
-from collections.abc import Callable
-from typing import Any, TypeVar
+from collections.abc import Callable, Iterable
+from dataclasses import dataclass
+from typing import Any
+
+Trace = list[tuple[str, tuple[str, ...]]]
 
 
 class PhaseNotReached(Exception):
-    """A requested phase isn't in this pipeline, or the stop excluded it."""
+    """A phase named in a request is not in the pipeline, or the stop point
+    leaves it out so the request can never be honoured."""
 
 
 class Phase(ABC):
-    """A named pipeline phase; `passes` is the step list `--trace` reports."""
+    """One named step of a pipeline; `passes` lists what `--trace` reports for it."""
 
     def __init__(self, name: str) -> None:
         self.name = name
@@ -34,7 +45,7 @@ class Phase(ABC):
 
 
 class CallablePhase(Phase):
-    """A phase that is a single callable; `passes` is supplied at construction."""
+    """A phase backed by a single function `module -> module`."""
 
     def __init__(self, name: str, fn: Callable[[Any], Any], passes: tuple[str, ...] = ()) -> None:
         super().__init__(name)
@@ -49,37 +60,83 @@ class CallablePhase(Phase):
         return self._fn(module)
 
 
-_P = TypeVar("_P", bound=Phase)
+@dataclass(frozen=True)
+class _Schedule:
+    """What one `run` call does: phases [0, count) run; `dump_before[i]` /
+    `dump_after[i]` say whether the module is printed around phase i."""
+
+    count: int
+    dump_before: tuple[bool, ...]
+    dump_after: tuple[bool, ...]
+
+
+def _banner(when: str, phase: str, module: Any) -> str:
+    return f"// ---- IR {when} phase '{phase}' ---- //\n{module}"
 
 
 class PhasePipeline:
-    """An ordered list of phases plus the `run` that folds a module through them."""
+    """Phases in execution order, addressable by name."""
 
     def __init__(self) -> None:
-        self._phases: list[Phase] = []
+        self._order: list[Phase] = []
+        self._index: dict[str, int] = {}
+
+    # -- building ------------------------------------------------------------
+
+    def _adopt(self, phases: Iterable[Phase]) -> None:
+        incoming = list(phases)
+        names = [p.name for p in incoming]
+        clash = {n for n in names if n in self._index or names.count(n) > 1}
+        if clash:
+            raise ValueError(f"phase name(s) already in the pipeline: {sorted(clash)}")
+        for p in incoming:
+            self._index[p.name] = len(self._order)
+            self._order.append(p)
 
     def add_callable_phase(
         self, name: str, fn: Callable[[Any], Any], passes: tuple[str, ...] = ()
     ) -> CallablePhase:
-        return self._append(CallablePhase(name, fn, passes))
-
-    def _append(self, phase: _P) -> _P:
-        if self.find(phase.name) is not None:
-            raise ValueError(f"duplicate phase name {phase.name!r}")
-        self._phases.append(phase)
+        phase = CallablePhase(name, fn, passes)
+        self._adopt([phase])
         return phase
 
     def extend(self, other: PhasePipeline) -> None:
-        for phase in other._phases:
-            if self.find(phase.name) is not None:
-                raise ValueError(f"duplicate phase name {phase.name!r}")
-        self._phases.extend(other._phases)
+        """Append every phase of `other`, keeping its order (all or none)."""
+        self._adopt(other._order)
+
+    # -- queries -------------------------------------------------------------
 
     def names(self) -> list[str]:
-        return [phase.name for phase in self._phases]
+        return [p.name for p in self._order]
 
     def find(self, name: str) -> Phase | None:
-        return next((phase for phase in self._phases if phase.name == name), None)
+        at = self._index.get(name)
+        return None if at is None else self._order[at]
+
+    # -- running -------------------------------------------------------------
+
+    def _schedule(self, stop_before, stop_after, print_before, print_after) -> _Schedule:
+        if stop_before and stop_after:
+            raise ValueError("give stop_before or stop_after, not both")
+        wanted = {n for n in (stop_before, stop_after) if n} | set(print_before) | set(print_after)
+        absent = sorted(n for n in wanted if n not in self._index)
+        if absent:
+            raise PhaseNotReached(f"no phase named {absent} in this pipeline {self.names()}")
+        if stop_before:
+            count = self._index[stop_before]
+        elif stop_after:
+            count = self._index[stop_after] + 1
+        else:
+            count = len(self._order)
+        cut = sorted(n for n in set(print_before) | set(print_after) if self._index[n] >= count)
+        if cut:
+            raise PhaseNotReached(f"phase(s) {cut} would be printed but the stop point skips them")
+        ran = self._order[:count]
+        return _Schedule(
+            count,
+            tuple(p.name in print_before for p in ran),
+            tuple(p.name in print_after for p in ran),
+        )
 
     def run(
         self,
@@ -91,30 +148,20 @@ class PhasePipeline:
         print_ir_before: frozenset[str] = frozenset(),
         print_ir_after: frozenset[str] = frozenset(),
         emit: Callable[[str], None] = print,
-    ) -> tuple[Any, list[tuple[str, tuple[str, ...]]]]:
-        """Fold `module` through the phases; returns (module, [(phase, passes), ...])."""
-        if stop_before and stop_after:
-            raise ValueError("stop_before and stop_after are mutually exclusive")
-        names = self.names()
-        referenced = {n for n in (stop_before, stop_after) if n}
-        referenced |= set(print_ir_before) | set(print_ir_after)
-        unknown = referenced - set(names)
-        if unknown:
-            raise PhaseNotReached(f"unknown phase(s) {sorted(unknown)}; phases: {names}")
-        end = len(self._phases)
-        if stop_before:
-            end = names.index(stop_before)
-        elif stop_after:
-            end = names.index(stop_after) + 1
-        missed = (set(print_ir_before) | set(print_ir_after)) - set(names[:end])
-        if missed:
-            raise PhaseNotReached(f"can't print at phase(s) {sorted(missed)}; the stop excludes them")
-        trace: list[tuple[str, tuple[str, ...]]] = []
-        for phase in self._phases[:end]:
-            if phase.name in print_ir_before:
-                emit(f"// -----// IR before {phase.name} //----- //\n{module}")
+    ) -> tuple[Any, Trace]:
+        """Pass `module` through the phases up to the stop point.
+
+        Returns the final module and the trace [(phase name, passes), ...] of
+        the phases that ran. Raises PhaseNotReached for an unknown phase name
+        or a print request past the stop, ValueError for two stops."""
+        sched = self._schedule(stop_before, stop_after, print_ir_before, print_ir_after)
+        trace: Trace = []
+        for i in range(sched.count):
+            phase = self._order[i]
+            if sched.dump_before[i]:
+                emit(_banner("before", phase.name, module))
             module = phase.run(module, get_context)
             trace.append((phase.name, tuple(phase.passes)))
-            if phase.name in print_ir_after:
-                emit(f"// -----// IR after {phase.name} //----- //\n{module}")
+            if sched.dump_after[i]:
+                emit(_banner("after", phase.name, module))
         return module, trace

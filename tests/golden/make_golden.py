@@ -1,10 +1,10 @@
 """Regenerates the golden fixtures in this directory from the reference's own files.
 
-    python tests/golden/make_golden.py [REFERENCE_ROOT]
+    python tests/golden/make_golden.py REFERENCE_ROOT
 
-Reads plain-text artifacts of rdadolf/ml-reentry-mlir (default root:
-/root/reference) and writes small .npz files; nothing at test time reads the
-reference tree. Fixtures:
+Reads plain-text artifacts of rdadolf/ml-reentry-mlir from a checkout at
+REFERENCE_ROOT (required) and writes small .npz files; nothing at test time
+reads the reference tree. Fixtures:
 
   gcn_toy.npz       conv1/conv2 weights and biases of the GCN toy model, decoded
                     from the dense_resource blobs of test/reference/gcn.raw.mlir:26-35
@@ -109,4 +109,6 @@ def main(root: Path) -> None:
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference"))
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py REFERENCE_ROOT (a checkout of rdadolf/ml-reentry-mlir)")
+    main(Path(sys.argv[1]))

@@ -99,6 +99,26 @@ def test_gcn_aggregate_log_softmax_epilogue(device):
     assert_close(out, ref)
 
 
+def test_elu_keeps_relative_accuracy_near_zero(device):
+    """ELU of small negative sums (|v| < 1e-3) is expm1(v) to a relative 1e-4
+    with no absolute slack: exp(v) - 1 would cancel there."""
+    from gnnc.b200 import runtime as rt
+
+    n = 3000
+    ei = random_graph(n, 30000, 17, heavy=((4, 2000),))
+    rowptr, col, mult = rt.csr_from_coo(ei.to(device), n, self_loops=True, dedupe=True)
+    _, _, w = rt.gcn_norm(rowptr, col, mult)
+    g = torch.Generator().manual_seed(17)
+    # strictly negative features: every row sum is negative and below 1e-3 in size
+    h_host = -(torch.rand(n, 64, generator=g) * 5e-5 + 1e-8)
+    h = rt.empty_rows(n, 64, torch.float32, device)
+    h.copy_(h_host)
+    out = rt.gcn_aggregate(_plan(rowptr), rowptr, col, w, h, act=rt.ACT_ELU).double().cpu()
+    agg = O.gcn_rows_fp64(rowptr.cpu(), col.cpu(), w.cpu(), h_host.double())
+    assert float(agg.abs().max()) < 1e-3 and bool((agg < 0).all())
+    np.testing.assert_allclose(out.numpy(), torch.expm1(agg).numpy(), rtol=1e-4, atol=0)
+
+
 def _gat_case(device, n, e, H, C, dtype, heavy, cta, split, concat, act, lsm, seed,
               self_loops=True, out_dtype=torch.float32, equal_logits=False):
     from gnnc.b200 import runtime as rt

@@ -29,7 +29,10 @@ def test_phase_pipeline_stop_and_print():
     assert p.run(1, stop_before="b")[0] == 2
     seen = []
     p.run(1, print_ir_after=frozenset({"a"}), emit=seen.append)
-    assert "IR after a" in seen[0] and seen[0].endswith("2")
+    assert "IR after phase 'a'" in seen[0] and seen[0].endswith("2")
+    seen.clear()
+    p.run(1, print_ir_before=frozenset({"b"}), print_ir_after=frozenset({"c"}), emit=seen.append)
+    assert len(seen) == 2 and seen[0].endswith("2") and seen[1].endswith("17")
     with pytest.raises(PhaseNotReached):
         p.run(1, stop_after="zz")
     with pytest.raises(PhaseNotReached):
@@ -38,6 +41,12 @@ def test_phase_pipeline_stop_and_print():
         p.run(1, stop_before="a", stop_after="b")
     with pytest.raises(ValueError):
         p.add_callable_phase("a", lambda m: m)
+    q = PhasePipeline()
+    q.add_callable_phase("d", lambda m: m)
+    q.add_callable_phase("b", lambda m: m)
+    with pytest.raises(ValueError):  # all or none: "d" is not taken either
+        p.extend(q)
+    assert p.names() == ["a", "b", "c"] and p.find("d") is None
 
 
 @pytest.mark.parametrize("model_name", ["gcn", "gat", "sage"])
