@@ -17,24 +17,27 @@ cross NVLink (208 bytes a row instead of the 528 of h and a_src): the copy
 engines pull the other ranks' rows from their HBM (CUDA IPC mappings) in
 pieces on a side stream while the projection of the pieces already present
 runs, every rank projects all rows, and each rank aggregates its own rows with
-the single-GPU plan's split decisions (rows identical to one GPU's, checked by
---check). --exchange selects the alternatives: needed (only the remote rows a
-rank's edges read), input (NCCL all-gather of X), output (project own rows,
-all-gather h and a_src).
+the single-GPU plan's split decisions.
 
 Printed (rank 0, one JSON line): value = stored edges x steps / device time
 (max over ranks); e2e = the same metric through gnnc.execution.run_jit with
 host inputs (pinned X copied in and the output copied out every step; the
 graph stays resident on the device after the first call); roofline of the
-aggregation kernel from its CUDA-event duration; cpu_baseline = the CPU
-oracle's PyG-style op sequence on a bounded row sample (rank 0, N = 1).
+aggregation kernel (DRAM bytes of the committed ncu capture of this build's
+kernel source over its CUDA-event duration, beside the edge-gather byte
+model); cpu_baseline = the CPU oracle's PyG-style op sequence on a bounded row
+sample (rank 0, N = 1); check = at N = 1 the layer's rows against the CPU
+oracle (float64, every hub row plus a seeded sample), at N > 1 every rank's
+rows against the same layer computed on one GPU (bit-exact).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload c4-gat-layer1|c5-fused-rmat24]
 """
 
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
 import math
 import os
@@ -55,11 +58,20 @@ import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
 WORKLOAD = "c4-gat-layer1"
+C5 = "c5-fused-rmat24"
 HEADS, CH, IN = 4, 64, 100
 F = HEADS * CH
 METRIC = "edges/sec per fused GCN/GAT layer at 1/2/4/8 B200; % of HBM roofline"
 FALLBACK_HBM_GBS = 6650.0
-TRAFFIC_FILE = ROOT / "profiles" / "gat_aggregate_c4_layer1.txt"
+# DRAM traffic of one full-size aggregation launch, captured with ncu for the
+# kernel source whose hash the file records (profiles/<kernel>_<workload>.txt)
+TRAFFIC_FILES = {WORKLOAD: ROOT / "profiles" / "gat_aggregate_c4_layer1.txt",
+                 C5: ROOT / "profiles" / "gat_aggregate_c5_rmat24.txt"}
+KERNEL_SOURCES = ("ml-reentry-mlir_b200/csrc/aggregate.cu", "ml-reentry-mlir_b200/csrc/common.cuh")
+# parity sample: every row above this in-degree plus this many seeded rows
+HUB_DEGREE = 1024
+SAMPLE_ROWS = 50_000
+BF16_TOL = 2e-2
 
 
 # ---------------------------------------------------------------------------
@@ -74,7 +86,9 @@ def log(*a) -> None:
 def algorithmic_bytes(E: int, N: int, F: int = F, H: int = HEADS, s_h: int = 2, s_out: int = 2) -> int:
     """Edge-gather byte model of one fused GAT aggregation launch: per edge the
     column index, the h[src] row and a_src[src]; per destination row its rowptr
-    entry, a_dst and the output row."""
+    entry, a_dst and the output row. Every gathered row counts, including the
+    ones L2 serves, so on a graph whose hub rows stay in L2 it exceeds the DRAM
+    traffic."""
     return E * (4 + F * s_h + H * 4) + N * (4 + H * 4 + F * s_out)
 
 
@@ -88,14 +102,70 @@ def hbm_peak() -> tuple[float, str]:
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def ncu_traffic() -> tuple[int | None, str | None]:
-    """dram bytes per aggregation launch from the committed ncu summary, if present."""
-    if not TRAFFIC_FILE.exists():
-        return None, None
-    for line in TRAFFIC_FILE.read_text().splitlines():
+def kernel_source_hash() -> str:
+    h = hashlib.sha256()
+    for rel in KERNEL_SOURCES:
+        h.update((ROOT / rel).read_bytes())
+    return h.hexdigest()[:16]
+
+
+def ncu_traffic(workload: str) -> dict:
+    """DRAM bytes per full-size aggregation launch from the committed ncu
+    summary, used only when it was captured from the current kernel source."""
+    path = TRAFFIC_FILES[workload]
+    out = {"bytes": None, "file": f"profiles/{path.name}", "source_hash": None,
+           "current_source_hash": kernel_source_hash(), "current": False}
+    if not path.exists():
+        return out
+    for line in path.read_text().splitlines():
         if line.startswith("dram_bytes_per_launch_full_size:"):
-            return int(float(line.split(":", 1)[1].split()[0])), TRAFFIC_FILE.name
-    return None, None
+            out["bytes"] = int(float(line.split(":", 1)[1].split()[0]))
+        elif line.startswith("kernel_source_sha256_16:"):
+            out["source_hash"] = line.split(":", 1)[1].strip()
+    out["current"] = out["bytes"] is not None and out["source_hash"] == out["current_source_hash"]
+    return out
+
+
+def roofline(kernel: str, workload: str, bytes_alg: float, agg_ms: float, world: int) -> dict:
+    """Roofline of the aggregation kernel. Primary figure: measured DRAM bytes
+    per launch (ncu, this kernel source, one GPU) over the CUDA-event duration;
+    beside it the edge-gather model, an upper count that includes L2 hits."""
+    peak, peak_kind = hbm_peak()
+    t = agg_ms / 1e3
+    alg = bytes_alg / t / 1e9
+    tr = ncu_traffic(workload)
+    use_dram = tr["current"] and world == 1
+    line = {
+        "bound": "hbm",
+        "kernel": kernel,
+        "basis": "dram" if use_dram else "edge-gather (upper count: includes L2 hits)",
+        "achieved": None,
+        "peak": peak,
+        "peak_source": (f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
+                        else "fallback 6.65 TB/s"),
+        "unit": "GB/s",
+        "frac": None,
+        "traffic": tr["bytes"] if use_dram else None,
+        "traffic_source": {**tr, "note": (
+            "ncu dram__bytes_read.sum + dram__bytes_write.sum, one full-size launch on one GPU"
+            if world == 1 else
+            "not used: the capture is of the one-GPU launch, not of this rank's share")},
+        "launch_ms": agg_ms,
+        "algorithmic": {
+            "bytes_per_launch": bytes_alg,
+            "achieved": alg,
+            "frac": alg / peak,
+            "model": "E*(4 + F*2 + H*4) + N*(4 + H*4 + F*2), F=256, H=4 (edge-gather)",
+            "note": "counts every gathered h row, including those L2 serves: an upper count "
+                    "of the bytes, not DRAM traffic; it can exceed the copy peak",
+        },
+    }
+    if use_dram:
+        dram = tr["bytes"] / t / 1e9
+        line.update(achieved=dram, frac=dram / peak, achieved_dram=dram, frac_dram=dram / peak)
+    else:
+        line.update(achieved=alg, frac=alg / peak, achieved_dram=None, frac_dram=None)
+    return line
 
 
 class ClockSampler:
@@ -225,159 +295,59 @@ def broadcast_workload(rank, world, device, scale=1.0):
     return cfg, ei, x, ei_d, x_d
 
 
+
+
 # ---------------------------------------------------------------------------
 # b200 arm
 # ---------------------------------------------------------------------------
 
 
-class NeededExchange:
-    """Layer on `world` ranks moving only the remote input rows this rank's
-    edges read (partition.NeededRows); the local CSR's columns are relabelled
-    to compact-table rows. Two ways to move them:
+class OneGpu:
+    """The layer on one GPU: project every row, aggregate every row."""
 
-    * read="copy": each owner packs, per requester, the rows it needs into one
-      block of its exported pack buffer (gnnc_gather_rows); each requester
-      pulls one block per owner with the copy engines into its compact table,
-      pipelined with the projection. Three one-word NCCL all-reduces per step
-      order the owners' input writes, their packs and the peers' reads.
-    * read="gather": each requester gathers the rows straight from the owners'
-      mapped input blocks (gnnc_gather_rows with plain loads over NVLink: no
-      pack, no third fence), then projects its own and the gathered rows."""
+    def __init__(self, rt, rowptr, col, x_d, W, att_s, att_d, device):
+        from gnnc.b200.program import to_device_features
 
-    PIECE_ROWS = 1 << 18
-
-    def __init__(self, P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device,
-                 read="copy"):
         N = x_d.size(0)
-        self.P, self.rt, self.N, self.read = P, rt, N, read
-        self.rr = rr = P.row_range(N, world, rank)
-        rowptr_l, col_l = P.local_csr(rowptr, col, rr)
-        self.need = need = P.NeededRows(col_l, rr)
-        self.rowptr_l, self.col_l = rowptr_l, need.col
-        self.n_loc = rr.count
-        self.ld = ld = rt.row_stride(IN, torch.bfloat16)
-        R = rr.rows_per_rank
-        self.x_own = torch.zeros((R, ld), dtype=torch.bfloat16, device=device)
-        self.x_own[: rr.count, :IN] = x_d[rr.begin : rr.end]
-        if read == "gather":
-            self.pack = None
-            self.peers = P.PeerRows(self.x_own, rr, N)
-        else:
-            self.pack = torch.zeros((max(1, need.pack_rows), ld), dtype=torch.bfloat16,
-                                    device=device)
-            self.peers = P.PeerBuffers(self.pack)
-        nc = need.compact_rows
-        self.xc = torch.zeros((max(1, nc - R), ld), dtype=torch.bfloat16, device=device)
-        self.h_full = rt.empty_rows(nc, F, torch.bfloat16, device)
-        self.a_full = torch.empty((nc, HEADS), dtype=torch.float32, device=device)
-        self.d_own = torch.empty((R, HEADS), dtype=torch.float32, device=device)
-        self.adst_l = self.d_own[: rr.count]
-        self.n_src = nc
-        self.W, self.att_s, self.att_d = W, att_s, att_d
-        self.fence_buf = torch.zeros(1, dtype=torch.int32, device=device)
-        self.pieces = []
-        for p in P.read_order(rr)[1:]:
-            n_p = need.need_rows[p]
-            for a in range(0, n_p, self.PIECE_ROWS):
-                self.pieces.append((p, a, min(n_p, a + self.PIECE_ROWS)))
-        self.side = torch.cuda.Stream(device)
-        self.piece_ev = [torch.cuda.Event() for _ in self.pieces]
-        remote = max(1, N - rr.count)
-        share = f"{sum(need.need_rows) / remote:.0%} of the remote rows here"
-        if read == "gather":
-            self.order = P.read_order(rr)[1:]
-            n_gathers = sum(1 for p in self.order if need.need_rows[p])
-            self.proj_launches = n_gathers + 2  # gathers + own and remote projections
-            self.describe = (f"requesters gather only the remote input rows their edges read "
-                             f"({share}) from the owners' mapped blocks with plain loads over "
-                             "NVLink (CUDA IPC), then project own and gathered rows")
-        else:
-            self.proj_launches = 1 + len(self.pieces) + 1  # projections + the pack
-            self.describe = (f"owners pack, requesters pull only the remote input rows their "
-                             f"edges read ({share}) over NVLink with the copy engines (CUDA IPC), "
-                             "pipelined with the projection")
+        self.rt, self.W, self.att_s, self.att_d = rt, W, att_s, att_d
+        self.rowptr_l, self.col_l = rowptr, col
+        self.n_loc = self.n_src = N
+        self.x = to_device_features(x_d, torch.bfloat16, device)
+        self.h_full = rt.empty_rows(N, F, torch.bfloat16, device)
+        self.a_full = torch.empty((N, HEADS), dtype=torch.float32, device=device)
+        self.adst_l = torch.empty((N, HEADS), dtype=torch.float32, device=device)
+        self.proj_launches = 1
+        self.describe = "one GPU"
 
     def x_local_rows(self):
-        return self.x_own[: self.n_loc, :IN]
+        return self.x
 
     def node_ids(self):
-        return torch.arange(self.rr.begin, self.rr.end)
-
-    def fence(self):
-        dist.all_reduce(self.fence_buf)
-
-    def _proj(self, x, rows: slice, adst):
-        self.rt.proj(x, self.W, att_src=self.att_s, att_dst=self.att_d, heads=HEADS,
-                     out_dtype=torch.bfloat16, out=self.h_full[rows], asrc_out=self.a_full[rows],
-                     adst_out=adst)
+        return torch.arange(self.n_loc)
 
     def project(self):
-        if self.read == "gather":
-            return self._project_gather()
-        need, rt, R = self.need, self.rt, self.rr.rows_per_rank
-        self.fence()  # every rank's input rows are written
-        if need.pack_rows:
-            rt.gather_rows(self.x_own, need.pack_idx, self.pack)
-        self.fence()  # every rank's packs are written
-        cur = torch.cuda.current_stream()
-        self.side.wait_stream(cur)
-        row_bytes = self.ld * 2
-        with torch.cuda.stream(self.side):
-            for (p, a, b), ev in zip(self.pieces, self.piece_ev):
-                off = need.remote_off[p]
-                rt.peer_copy(self.xc[need.base[p] - R + a :], self.peers.rows(p, off + a, off + b),
-                             (b - a) * row_bytes)
-                ev.record(self.side)
-        n = self.n_loc
-        self._proj(self.x_own[:n, :IN], slice(0, n), self.d_own[:n])
-        for (p, a, b), ev in zip(self.pieces, self.piece_ev):
-            cur.wait_event(ev)
-            lo = need.base[p] + a
-            xs = self.xc[lo - R : lo - R + (b - a), :IN]
-            # a_dst of remote rows is not used: it goes to a scratch buffer
-            self._proj(xs, slice(lo, lo + (b - a)), self._dscratch(b - a))
-        self.fence()  # every rank is done reading the packs
-
-    def _project_gather(self):
-        need, rt, R = self.need, self.rt, self.rr.rows_per_rank
-        self.fence()  # every rank's input rows are written
-        for p in self.order:  # rotated: each owner serves one requester at a time
-            if need.need_rows[p]:
-                lo = need.base[p] - R
-                rt.gather_rows(self.peers.view(p, IN), need.need_idx[p], self.xc[lo:])
-        self.fence()  # every rank is done reading the owners' blocks
-        n = self.n_loc
-        self._proj(self.x_own[:n, :IN], slice(0, n), self.d_own[:n])
-        nr = need.compact_rows - R
-        if nr:
-            self._proj(self.xc[:nr, :IN], slice(R, R + nr), self._dscratch(nr))
-
-    def _dscratch(self, rows):
-        if getattr(self, "_ds", None) is None or self._ds.size(0) < rows:
-            self._ds = torch.empty((rows, HEADS), dtype=torch.float32, device=self.x_own.device)
-        return self._ds[:rows]
+        self.rt.proj(self.x, self.W, att_src=self.att_s, att_dst=self.att_d, heads=HEADS,
+                     out_dtype=torch.bfloat16, out=self.h_full, asrc_out=self.a_full,
+                     adst_out=self.adst_l)
 
     def close(self):
-        self.peers.close()
+        pass
 
 
 class PeerExchange:
-    """Layer on `world` ranks reading the remote input rows from the owners'
-    HBM: rank r owns rows [r*R, (r+1)*R) and their input rows; every rank maps
-    the others' input blocks (CUDA IPC). Remote rows are pulled by the copy
-    engines over NVLink (no SM used) into a local table, piece by piece on a
-    side stream, while the projection runs on the rows already present (its
-    own rows first); then the rank aggregates its own rows. With
-    read="tma" the projection's TMA loads read the mapped rows directly
-    instead (no staging copy). Two one-word NCCL all-reduces per step order
-    the input writes and the peers' reads."""
+    """The layer on `world` ranks, reading the remote input rows from the
+    owners' HBM: rank r owns rows [r*R, (r+1)*R) and their input rows; every
+    rank maps the others' input blocks (CUDA IPC). The copy engines pull the
+    remote rows over NVLink (no SM used) into a local table, piece by piece on
+    a side stream, while the projection runs on the rows already present (its
+    own rows first); then the rank aggregates its own rows. Two one-word NCCL
+    all-reduces per step order the input writes and the peers' reads."""
 
     PIECE_ROWS = 1 << 18
 
-    def __init__(self, P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device,
-                 read="copy"):
+    def __init__(self, P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device):
         N = x_d.size(0)
-        self.P, self.rt, self.N, self.read = P, rt, N, read
+        self.P, self.rt, self.N = P, rt, N
         self.rr = rr = P.row_range(N, world, rank)
         self.rowptr_l, self.col_l = P.local_csr(rowptr, col, rr)
         self.n_loc = rr.count
@@ -386,8 +356,7 @@ class PeerExchange:
         self.x_own = torch.zeros((R, ld), dtype=torch.bfloat16, device=device)
         self.x_own[: rr.count, :IN] = x_d[rr.begin : rr.end]
         self.peers = P.PeerRows(self.x_own, rr, N)
-        self.stage = (torch.empty((world * R, ld), dtype=torch.bfloat16, device=device)
-                      if read == "copy" else None)
+        self.stage = torch.empty((world * R, ld), dtype=torch.bfloat16, device=device)
         self.h_full = rt.empty_rows(world * R, F, torch.bfloat16, device)
         self.a_full = torch.empty((world * R, HEADS), dtype=torch.float32, device=device)
         self.d_full = torch.empty((world * R, HEADS), dtype=torch.float32, device=device)
@@ -395,20 +364,17 @@ class PeerExchange:
         self.n_src = N
         self.W, self.att_s, self.att_d = W, att_s, att_d
         self.fence_buf = torch.zeros(1, dtype=torch.int32, device=device)
-        self.order = P.read_order(rr)
         # (owner, first row, last row) pieces of the remote rows, in read order
         self.pieces = []
-        for p in self.order[1:]:
+        for p in P.read_order(rr)[1:]:
             n_p = P.row_range(N, world, p).count
             for a in range(0, n_p, self.PIECE_ROWS):
                 self.pieces.append((p, a, min(n_p, a + self.PIECE_ROWS)))
         self.side = torch.cuda.Stream(device)
         self.piece_ev = [torch.cuda.Event() for _ in self.pieces]
-        self.proj_launches = 1 + (len(self.pieces) if read == "copy" else world - 1)
-        self.describe = (
-            "copy-engine pull of remote input rows over NVLink (CUDA IPC peer mapping), "
-            "pipelined with the projection; no data collective" if read == "copy" else
-            "projection TMA loads read remote input rows over NVLink (CUDA IPC peer mapping)")
+        self.proj_launches = 1 + len(self.pieces)
+        self.describe = ("copy-engine pull of remote input rows over NVLink (CUDA IPC peer "
+                         "mapping), pipelined with the projection; no data collective")
 
     def x_local_rows(self):
         return self.x_own[: self.n_loc, :IN]
@@ -429,118 +395,20 @@ class PeerExchange:
         self.fence()  # every rank's input rows are written
         cur = torch.cuda.current_stream()
         own = self.rr.rank
-        if self.read == "copy":
-            self.side.wait_stream(cur)
-            with torch.cuda.stream(self.side):
-                for (p, a, b), ev in zip(self.pieces, self.piece_ev):
-                    rt.peer_copy(self.stage[p * R + a :], self.peers.view(p, IN)[a:b],
-                                 (b - a) * self.ld * 2)
-                    ev.record(self.side)
-            self._proj(self.x_own[: self.n_loc, :IN], slice(own * R, own * R + self.n_loc))
+        self.side.wait_stream(cur)
+        with torch.cuda.stream(self.side):
             for (p, a, b), ev in zip(self.pieces, self.piece_ev):
-                cur.wait_event(ev)
-                self._proj(self.stage[p * R + a : p * R + b, :IN], slice(p * R + a, p * R + b))
-        else:
-            for p in self.order:
-                xv = self.peers.view(p, IN)
-                self._proj(xv, slice(p * R, p * R + xv.rows))
+                rt.peer_copy(self.stage[p * R + a :], self.peers.view(p, IN)[a:b],
+                             (b - a) * self.ld * 2)
+                ev.record(self.side)
+        self._proj(self.x_own[: self.n_loc, :IN], slice(own * R, own * R + self.n_loc))
+        for (p, a, b), ev in zip(self.pieces, self.piece_ev):
+            cur.wait_event(ev)
+            self._proj(self.stage[p * R + a : p * R + b, :IN], slice(p * R + a, p * R + b))
         self.fence()  # every rank is done reading (the owners may overwrite)
 
     def close(self):
         self.peers.close()
-
-
-class InputExchange:
-    """Layer on `world` ranks exchanging the input: X is all-gathered piece by
-    piece (block-cyclic row ownership) on a side stream while the projection of
-    the pieces already received runs; every rank projects all rows and
-    aggregates its own."""
-
-    def __init__(self, P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, chunks, device):
-        N = x_d.size(0)
-        self.P, self.rt = P, rt
-        self.rb = rb = P.row_blocks(N, world, rank, chunks)
-        self.world = world
-        self.rowptr_l, self.col_l = P.local_csr_blocks(rowptr, col, rb)
-        self.n_loc = rb.count
-        ld = rt.row_stride(IN, torch.bfloat16)
-        self.x_loc = P.local_blocks(rb, ld, torch.bfloat16, device)
-        self.x_loc[: rb.count, :IN] = x_d[rb.node_ids().to(device)]
-        self.x_tab = self.x_loc if world == 1 else P.input_table(rb, ld, torch.bfloat16, device)
-        self.h_full = rt.empty_rows(rb.padded_rows, F, torch.bfloat16, device)
-        self.a_full = torch.empty((rb.padded_rows, HEADS), dtype=torch.float32, device=device)
-        self.d_full = torch.empty((rb.padded_rows, HEADS), dtype=torch.float32, device=device)
-        self.adst_l = torch.empty((rb.count, HEADS), dtype=torch.float32, device=device)
-        self.n_src = N
-        self.W, self.att_s, self.att_d = W, att_s, att_d
-        self.comm = torch.cuda.Stream(device) if world > 1 else None
-        self.piece_ev = [torch.cuda.Event() for _ in range(chunks)]
-        self.proj_launches = chunks
-        self.describe = (f"NCCL all-gather of X in {chunks} pieces overlapped with the projection "
-                         "(block-cyclic rows; every rank projects all rows)")
-
-    def x_local_rows(self):
-        return self.x_loc[: self.n_loc, :IN]
-
-    def node_ids(self):
-        return self.rb.node_ids()
-
-    def project(self):
-        rb, P, rt = self.rb, self.P, self.rt
-        cur = torch.cuda.current_stream()
-        if self.comm is not None:
-            self.comm.wait_stream(cur)
-            with torch.cuda.stream(self.comm):
-                for c in range(rb.chunks):
-                    P.gather_piece(self.x_tab, self.x_loc, rb, c)
-                    self.piece_ev[c].record(self.comm)
-        for c in range(rb.chunks):
-            if self.comm is not None:
-                cur.wait_event(self.piece_ev[c])
-            sl = rb.piece(c)
-            rt.proj(self.x_tab[sl, :IN], self.W, att_src=self.att_s, att_dst=self.att_d,
-                    heads=HEADS, out_dtype=torch.bfloat16, out=self.h_full[sl],
-                    asrc_out=self.a_full[sl], adst_out=self.d_full[sl])
-        if self.world == 1:
-            self.adst_l = self.d_full[: self.n_loc]
-        else:
-            self.adst_l.copy_(P.owned_rows(self.d_full, rb))
-
-
-class OutputExchange:
-    """Layer on `world` ranks exchanging the output: each rank projects its own
-    contiguous rows into its slot of the h / a_src tables, which are then
-    all-gathered."""
-
-    def __init__(self, P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device):
-        N = x_d.size(0)
-        self.P, self.rt = P, rt
-        self.rr = rr = P.row_range(N, world, rank)
-        self.rowptr_l, self.col_l = P.local_csr(rowptr, col, rr)
-        self.n_loc = rr.count
-        self.X_l = rt.empty_rows(rr.count, IN, torch.bfloat16, device)
-        self.X_l.copy_(x_d[rr.begin : rr.end])
-        self.h_full = P.gathered_table(rr, F, torch.bfloat16, device)
-        self.a_full = P.gathered_table(rr, HEADS, torch.float32, device)
-        self.adst_l = torch.empty((rr.count, HEADS), dtype=torch.float32, device=device)
-        self.n_src = N
-        self.W, self.att_s, self.att_d = W, att_s, att_d
-        self.proj_launches = 1
-        self.describe = "NCCL all-gather of h and a_src"
-
-    def x_local_rows(self):
-        return self.X_l
-
-    def node_ids(self):
-        return torch.arange(self.rr.begin, self.rr.end)
-
-    def project(self):
-        rr, P = self.rr, self.P
-        self.rt.proj(self.X_l, self.W, att_src=self.att_s, att_dst=self.att_d, heads=HEADS,
-                     out_dtype=torch.bfloat16, out=P.my_rows(self.h_full, rr),
-                     asrc_out=P.my_rows(self.a_full, rr), adst_out=self.adst_l)
-        P.all_gather_rows(self.h_full, rr)
-        P.all_gather_rows(self.a_full, rr)
 
 
 def run_b200(args) -> None:
@@ -569,25 +437,19 @@ def run_b200(args) -> None:
     att_s = conv.att_src.detach().reshape(-1).to(device)
     att_d = conv.att_dst.detach().reshape(-1).to(device)
     bias = conv.bias.detach().to(device)
-    chunks = args.chunks or (1 if world == 1 else 4)
-    if args.exchange == "needed" and world > 1:
-        lay = NeededExchange(P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device,
-                             read="gather" if args.peer_read == "gather" else "copy")
-    elif args.exchange == "peer" and world > 1:
+    if world > 1:
         if args.piece_rows:
             PeerExchange.PIECE_ROWS = args.piece_rows
-        lay = PeerExchange(P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device,
-                           read=args.peer_read)
-    elif args.exchange in ("input", "peer"):
-        lay = InputExchange(P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, chunks, device)
+        lay = PeerExchange(P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device)
     else:
-        lay = OutputExchange(P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device)
-    full = (rowptr, col, x_d) if args.check else None
+        lay = OneGpu(rt, rowptr, col, x_d, W, att_s, att_d, device)
+    full = (rowptr, col, x_d) if (args.check and world > 1) else None
     split = args.split_threshold
     if world > 1 and split == 0:
         # split the rows the single-GPU plan splits: bit-identical rows at every N
         sms = torch.cuda.get_device_properties(device).multi_processor_count
         split = P.whole_graph_split_threshold(col.numel(), sms)
+    host_csr = (rowptr.cpu(), col.cpu()) if (rank == 0 and world == 1) else None
     del rowptr, col, x_d
     rowptr_l, col_l = lay.rowptr_l, lay.col_l
     n_loc, e_loc = lay.n_loc, col_l.numel()
@@ -648,15 +510,15 @@ def run_b200(args) -> None:
     agg_worst, bytes_worst = float(g[worst, 1]), float(g[worst, 3])
 
     check = None
-    if args.check:
+    if full is not None:
         check = check_rows(rt, lay, full, W, att_s, att_d, bias, out_l, device)
         log(f"[bench] rank {rank}: own rows vs the single-GPU layer: {check}")
         full = None
-        if world > 1:  # the line reports every rank's verdict
-            verdicts: list = [None] * world
-            dist.all_gather_object(verdicts, check)
-            bad = [r for r, v in enumerate(verdicts) if v != "bit-exact"]
-            check = "bit-exact" if not bad else f"MISMATCH on ranks {bad}"
+        verdicts: list = [None] * world
+        dist.all_gather_object(verdicts, check)
+        bad = [r for r, v in enumerate(verdicts) if v != "bit-exact"]
+        check = {"kind": "every rank's rows vs the same layer on one GPU",
+                 "verdict": "bit-exact" if not bad else f"MISMATCH on ranks {bad}"}
 
     # ---- end to end through the public API (host buffers, copies timed) ----
     e2e = None
@@ -666,11 +528,9 @@ def run_b200(args) -> None:
 
     clocks = sampler.summary() if sampler else None
     if rank == 0:
-        peak, peak_kind = hbm_peak()
-        achieved = bytes_worst / (agg_worst / 1e3) / 1e9
-        traffic, traffic_src = ncu_traffic()
-        cpu = None if (world > 1 or args.no_cpu_baseline) else cpu_baseline(
-            ei_host, x_host, layer, target_seconds=args.cpu_seconds)
+        cpu = None
+        if world == 1:
+            cpu, check = cpu_leg(host_csr, ei_host, x_host, layer, out_l, args)
         launches_per_step = lay.proj_launches + 1 + (1 if info["n_split_rows"] > 0 else 0)
         line = {
             "metric": METRIC,
@@ -694,27 +554,14 @@ def run_b200(args) -> None:
                 "edges_without_self_loops": E - N,
                 "parallelism": f"dst-row partition x{world}" + (f" + {lay.describe}" if world > 1 else ""),
                 "l2": "inputs larger than L2 (h table 1.25 GB, X 0.51 GB; L2 126 MB): no flush",
-                "exchange": args.exchange if world > 1 else None,
                 "check": check,
-                "chunks": chunks if world > 1 else None,
                 "plan": info,
             },
             "nodes_per_s": N * K / (total_max / 1e3),
             "layer_ms": {"projection": float(g[worst, 2]), "aggregation": agg_worst,
                          "step": total_max / K},
-            "roofline": {
-                "bound": "hbm",
-                "kernel": "gnnc_gat_aggregate (agg_kernel + merge_kernel)",
-                "achieved": achieved,
-                "peak": peak,
-                "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback 6.65 TB/s",
-                "unit": "GB/s",
-                "frac": achieved / peak,
-                "traffic": traffic,
-                "traffic_source": traffic_src,
-                "algorithmic_bytes_per_launch": bytes_worst,
-                "bytes_model": "E*(4 + F*2 + H*4) + N*(4 + H*4 + F*2), F=256, H=4",
-            },
+            "roofline": roofline("gnnc_gat_aggregate (agg_kernel + merge_kernel)", WORKLOAD,
+                                 bytes_worst, agg_worst, world),
             "gpu_launches": launches_per_step * K,
             "clocks": clocks,
             "e2e": e2e,
@@ -723,10 +570,9 @@ def run_b200(args) -> None:
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
-        if hasattr(lay, "close"):
-            torch.cuda.synchronize(device)
-            lay.close()
-            dist.barrier()
+        torch.cuda.synchronize(device)
+        lay.close()
+        dist.barrier()
         dist.destroy_process_group()
 
 
@@ -829,8 +675,9 @@ def run_c5(args) -> None:
     ms_max = float(gs[worst, 0])
     clocks = sampler.summary() if sampler else None
     if rank == 0:
-        peak, peak_kind = hbm_peak()
-        achieved = float(gs[worst, 1]) / (ms_max / K / 1e3) / 1e9
+        cpu = check = None
+        if world == 1:
+            cpu, check = cpu_leg_c5(rowptr_l, col_l, h, asrc, adst_l, out_l, info, args)
         line = {
             "metric": METRIC,
             "value": E * K / (ms_max / 1e3),
@@ -845,7 +692,7 @@ def run_c5(args) -> None:
             "dtype": "bf16",
             "data": "synthetic (seeded R-MAT scale 24 on the device, seeded N(0,1) features)",
             "config": {
-                "workload": "c5-fused-rmat24",
+                "workload": C5,
                 "op": "fused SDDMM -> LeakyReLU(0.2) -> edge softmax -> SpMM, 4 heads x 64, "
                       "bf16 h, fp32 accumulation, bf16 out",
                 "nodes": N,
@@ -855,24 +702,15 @@ def run_c5(args) -> None:
                 "l2": "inputs larger than L2 (h table 8.6 GB; L2 126 MB): no flush",
                 "plan_rank0": info,
                 "edges_per_rank": [int(v) for v in gs[:, 2].tolist()],
+                "check": check,
             },
-            "roofline": {
-                "bound": "hbm",
-                "kernel": "gnnc_gat_aggregate (agg_kernel + merge_kernel)",
-                "achieved": achieved,
-                "peak": peak,
-                "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback 6.65 TB/s",
-                "unit": "GB/s",
-                "frac": achieved / peak,
-                "traffic": None,
-                "algorithmic_bytes_per_launch": float(gs[worst, 1]),
-                "bytes_model": "E*(4 + F*2 + H*4) + N*(4 + H*4 + F*2), F=256, H=4",
-            },
+            "roofline": roofline("gnnc_gat_aggregate (agg_kernel + merge_kernel)", C5,
+                                 float(gs[worst, 1]), ms_max / K, world),
             "gpu_launches": (1 + (1 if info["n_split_rows"] > 0 else 0)) * K,
             "clocks": clocks,
             "e2e": None,
             "e2e_note": "not measured for the microbenchmark (a 9 GB h table per step would time PCIe)",
-            "cpu_baseline": None,
+            "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -886,14 +724,12 @@ def check_rows(rt, lay, full, W, att_s, att_d, bias, out_l, device) -> str:
     from gnnc.b200.program import to_device_features
 
     rowptr, col, x_d = full
-    N = x_d.size(0)
     X = to_device_features(x_d, torch.bfloat16, device)
     h, a, d = rt.proj(X, W, att_src=att_s, att_dst=att_d, heads=HEADS, out_dtype=torch.bfloat16)
     out = rt.gat_aggregate(rt.Plan(rowptr), rowptr, col, h, a, d, heads=HEADS, concat=True,
                            bias=bias, act=rt.ACT_ELU, out_dtype=torch.bfloat16)
     ids = lay.node_ids().to(device)
     same = torch.equal(out[ids].contiguous(), out_l.contiguous())
-    del N
     return "bit-exact" if same else "MISMATCH"
 
 
@@ -925,7 +761,7 @@ def e2e_b200(args, layer, ei_host, x_host, device, world, N, E, project, aggrega
         d2h = out.numel() * out.element_size()
         api = "gnnc.execution.run_jit(compile_executable(GATConv+ELU, target='b200'), (x, edge_index))"
     else:
-        # Per rank: pinned host X rows in, layer (incl. the all-gather), output rows out.
+        # Per rank: pinned host X rows in, layer (incl. the exchange), output rows out.
         x_dev = lay.x_local_rows()
         x_pin = torch.empty(tuple(x_dev.shape), dtype=torch.bfloat16, pin_memory=True)
         x_pin.copy_(x_dev.cpu())
@@ -964,14 +800,14 @@ def e2e_b200(args, layer, ei_host, x_host, device, world, N, E, project, aggrega
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline / reference arm
+# CPU leg (rank 0, one GPU): the oracle as baseline and as checker
 # ---------------------------------------------------------------------------
 
 
 class CpuSample:
     """The oracle's PyG-style GAT layer on a bounded sample of destination rows."""
 
-    def __init__(self, ei, x, layer):
+    def __init__(self, rowptr, col, x, layer):
         from oracle import gnn_oracle as O
 
         self.O = O
@@ -979,16 +815,8 @@ class CpuSample:
         self.cores = torch.get_num_threads()
         N = x.size(0)
         t0 = time.time()
-        # CSR by destination with one self-loop per node (GATConv's add_self_loops),
-        # sorted with torch (set-up, not timed)
-        keep = ei[0] != ei[1]
-        loops = torch.arange(N, dtype=torch.int64)
-        src = torch.cat([ei[0][keep], loops])
-        dst = torch.cat([ei[1][keep], loops])
-        key = torch.sort(dst * N + src).values
-        self.col = key % N
-        self.rowptr = torch.zeros(N + 1, dtype=torch.int64)
-        self.rowptr[1:] = torch.cumsum(torch.bincount(key // N, minlength=N), 0)
+        self.rowptr = rowptr.to(torch.int64)
+        self.col = col
         conv = layer.conv1
         self.W = conv.lin.weight.detach().to(torch.bfloat16).float()
         self.att_s = conv.att_src.detach().float()
@@ -1021,8 +849,7 @@ class CpuSample:
         return self.rows_for(int(rate * seconds))
 
 
-def cpu_baseline(ei, x, layer, target_seconds: float = 15.0) -> dict:
-    s = CpuSample(ei, x, layer)
+def cpu_baseline(s: CpuSample, target_seconds: float) -> dict:
     rows = s.calibrate(target_seconds / 5)
     edges = 0
     t0 = time.perf_counter()
@@ -1043,13 +870,138 @@ def cpu_baseline(ei, x, layer, target_seconds: float = 15.0) -> dict:
     }
 
 
+def layer_parity(rowptr, col, x, layer, out_dev) -> dict:
+    """The GPU layer's rows against the oracle's float64 GATConv + ELU computed
+    from the same bf16 X and weights: every row of in-degree > HUB_DEGREE plus
+    SAMPLE_ROWS seeded rows; tolerance 2e-2 (bf16 features and output)."""
+    from oracle import parity as PY
+
+    t0 = time.time()
+    conv = layer.conv1
+    rows = PY.sample_rows(rowptr, sample=SAMPLE_ROWS, hub_degree=HUB_DEGREE, seed=0)
+    ref = PY.gat_conv_rows_fp64(
+        x, rowptr, col, rows, conv.lin.weight.detach().to(torch.bfloat16), conv.att_src.detach(),
+        conv.att_dst.detach(), conv.bias.detach(), HEADS, act="elu")
+    got = out_dev[rows.to(out_dev.device)].float().cpu()
+    res = PY.compare(got, ref, rtol=BF16_TOL, atol=BF16_TOL)
+    deg = rowptr.diff()[rows]
+    n_hub = int((deg > HUB_DEGREE).sum())
+    res.update(
+        kind="GPU rows vs the CPU oracle (float64 GATConv + ELU from the same bf16 X and weights)",
+        verdict="pass" if res["pass"] else "FAIL",
+        rows_checked=int(rows.numel()),
+        hub_rows=n_hub,
+        hub_degree_cutoff=HUB_DEGREE,
+        edges_checked=int(deg.sum()),
+        max_degree_checked=int(deg.max()),
+        sample=f"{n_hub} rows of in-degree > {HUB_DEGREE} + {SAMPLE_ROWS} rows drawn with seed 0",
+        seconds=round(time.time() - t0, 1),
+    )
+    log(f"[bench] parity vs oracle: {res['verdict']} max abs {res['max_abs_err']:.3g} "
+        f"on {res['rows_checked']} rows ({res['seconds']}s)")
+    return res
+
+
+def cpu_leg(dev_csr, ei_host, x_host, layer, out_dev, args):
+    """(cpu_baseline, parity): the oracle timed on a row sample, and the oracle
+    as checker of the GPU layer's rows (each unless switched off). The check
+    runs on a CSR sorted on the host, and first compares it with the one the
+    GPU built (gnnc_csr_from_coo) bit for bit."""
+    from oracle import parity as PY
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    rowptr, col = PY.csr_by_destination(ei_host, x_host.size(0))
+    parity = None
+    if args.check:
+        same = (torch.equal(rowptr, dev_csr[0].to(torch.int64))
+                and torch.equal(col, dev_csr[1].to(torch.int64)))
+        parity = layer_parity(rowptr, col, x_host, layer, out_dev)
+        parity["device_csr_equals_host_csr"] = same
+        if not same:
+            parity["verdict"] = "FAIL"
+            parity["pass"] = False
+    if args.no_cpu_baseline:
+        return None, parity
+    s = CpuSample(rowptr, col, x_host, layer)
+    return cpu_baseline(s, args.cpu_seconds), parity
+
+
+def cpu_leg_c5(rowptr_d, col_d, h, asrc, adst, out_dev, info, args):
+    """(cpu_baseline, parity) for the c5 microbenchmark: the oracle's fused
+    chain (no projection) on given h / a_src / a_dst, timed on a row sample
+    and checked against the GPU rows: the rows that hold the most edges (the
+    split hubs among them), plus a seeded sample."""
+    from oracle import gnn_oracle as O
+    from oracle import parity as PY
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    rowptr = rowptr_d.to(torch.int64).cpu()
+    col = col_d.cpu().to(torch.int64)
+    deg = rowptr.diff()
+    top = torch.topk(deg, 32).indices
+    rows = PY.sample_rows(rowptr, sample=SAMPLE_ROWS, hub_degree=1 << 40, seed=0,
+                          extra=top.tolist())
+    parity = cpu = None
+    t0 = time.time()
+    if args.check:
+        local, src, _ = PY._row_edges(rowptr, col, rows)
+        uniq, inv = torch.unique(src, return_inverse=True)
+        ud = uniq.to(h.device)
+        ref = PY.gat_rows_given_fp64(local, inv, h[ud].cpu(), asrc[ud].cpu(),
+                                     adst[rows.to(h.device)].cpu(), HEADS)
+        got = out_dev[rows.to(out_dev.device)].float().cpu()
+        parity = PY.compare(got, ref, rtol=BF16_TOL, atol=BF16_TOL)
+        parity.update(
+            kind="GPU rows vs the CPU oracle (float64 fused chain on the same bf16 h, fp32 a_src/a_dst)",
+            verdict="pass" if parity["pass"] else "FAIL",
+            rows_checked=int(rows.numel()),
+            edges_checked=int(deg[rows].sum()),
+            max_degree_checked=int(deg[rows].max()),
+            split_rows_in_plan=info["n_split_rows"],
+            sample=f"the 32 rows of highest in-degree + {SAMPLE_ROWS} rows drawn with seed 0",
+            seconds=round(time.time() - t0, 1),
+        )
+        log(f"[bench] c5 parity vs oracle: {parity['verdict']} max abs "
+            f"{parity['max_abs_err']:.3g} ({parity['seconds']}s)")
+    if args.no_cpu_baseline:
+        return cpu, parity
+    # baseline: the PyG op sequence on destination rows [0, R) (row-contiguous sample)
+    R = int(torch.searchsorted(rowptr, torch.tensor(4_000_000)).item())
+    e_r = int(rowptr[R])
+    src = col[:e_r]
+    uniq, inv = torch.unique(src, return_inverse=True)
+    ud = uniq.to(h.device)
+    h_u, a_u = h[ud].cpu().float(), asrc[ud].cpu()
+    ad = adst[:R].cpu()
+    lp = rowptr[: R + 1]
+    reps, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < args.cpu_seconds or reps == 0:
+        O.gat_aggregate_sample(lp, inv, h_u, a_u, ad, HEADS)
+        reps += 1
+    dt = time.perf_counter() - t0
+    cpu = {
+        "value": e_r * reps / dt,
+        "unit": "edges/s",
+        "cores": torch.get_num_threads(),
+        "kind": "port",
+        "sample": (f"destination rows [0,{R}) = {e_r} of {int(rowptr[-1])} edges, {reps} "
+                   f"repetitions in {dt:.1f}s: the oracle's PyG op sequence for the fused chain "
+                   "(index_select, leaky_relu, scatter_reduce amax, exp, scatter_add, div, "
+                   "scatter_add) in torch fp32 on the host cores"),
+    }
+    return cpu, parity
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     _, ei, x = host_workload()
     layer = make_layer_module()
-    s = CpuSample(ei, x, layer)
+    from oracle import parity as PY
+
+    rowptr, col = PY.csr_by_destination(ei, x.size(0))
+    s = CpuSample(rowptr, col, x, layer)
     rows = s.calibrate(args.ref_step_seconds)
     for _ in range(args.warmup):
         s.run(rows)
@@ -1093,42 +1045,31 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
-    ap.add_argument("--workload", default=WORKLOAD, choices=(WORKLOAD, "c5-fused-rmat24"),
+    ap.add_argument("--workload", default=WORKLOAD, choices=(WORKLOAD, C5),
                     help="the headline layer (default) or the c5 fused-aggregation microbenchmark")
     ap.add_argument("--cta-threshold", type=int, default=0)
     ap.add_argument("--split-threshold", type=int, default=0)
-    ap.add_argument("--exchange", default="peer", choices=("peer", "needed", "input", "output"),
-                    help="N>1: read remote input rows in the projection (default), "
-                         "all-gather the input X, or all-gather the projected h")
     ap.add_argument("--piece-rows", type=int, default=0,
-                    help="peer exchange: rows per pulled piece (default 2^18)")
-    ap.add_argument("--peer-read", default="copy", choices=("copy", "tma", "gather"),
-                    help="peer exchange: copy-engine staging (default) or direct TMA reads; "
-                         "needed exchange: owner packs + copy-engine pulls (copy, default) or "
-                         "requester-side gathers over NVLink (gather)")
-    ap.add_argument("--chunks", type=int, default=0,
-                    help="input exchange: all-gather pieces (default 1 on one GPU, else 4)")
+                    help="N>1: rows per copy-engine piece of the input-row pull (default 2^18)")
     ap.add_argument("--e2e-steps", type=int, default=30)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--ref-step-seconds", type=float, default=0.3)
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--check", action="store_true",
-                    help="compare each rank's output rows with the single-GPU layer (bit-exact)")
-    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-check", dest="check", action="store_false",
+                    help="skip the parity check (N=1: rows vs the CPU oracle; N>1: every "
+                         "rank's rows vs the single-GPU layer, bit-exact)")
+    ap.add_argument("--no-cpu-baseline", action="store_true",
+                    help="skip the CPU leg (the oracle timed on a row sample, and its parity check)")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--scale", type=float, default=1.0,
                     help="shrink the graph (profiling captures only; not a bench line)")
     args = ap.parse_args()
-    if args.peer_read == "gather" and args.exchange != "needed":
-        ap.error("--peer-read gather goes with --exchange needed")
-    if args.peer_read == "tma" and args.exchange != "peer":
-        ap.error("--peer-read tma goes with --exchange peer")
     if args.warmup < 3 and args.impl == "b200":
         log("[bench] warmup raised to 3 (minimum)")
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
-    elif args.workload != WORKLOAD:
+    elif args.workload == C5:
         run_c5(args)
     else:
         run_b200(args)

@@ -65,7 +65,10 @@ typedef struct gnnc_plan gnnc_plan_t;
 /* ------------------------------------------------------------------------ */
 
 /* Replaces the per-process MLIR context + JIT engine set-up
- * (gnnc/__init__.py:23-39, gnnc/execution/__init__.py:66-68). */
+ * (gnnc/__init__.py:23-39, gnnc/execution/__init__.py:66-68).
+ * Allocates the context's small device area and resolves the address of the
+ * fixed scratch of gnnc_gat_aggregate_noalloc (loading the library's device
+ * code on `device`). */
 GNNC_API int gnnc_init(int device, gnnc_ctx_t** out_ctx);
 GNNC_API int gnnc_destroy(gnnc_ctx_t* ctx);
 
@@ -258,11 +261,15 @@ GNNC_API int gnnc_softmax_aggregate(gnnc_ctx_t* ctx, const gnnc_plan_t* plan, co
  * the process exits. A plan whose split rows need more than 16 MiB - 256 B of
  * partials (n_segments * (32 + F_pad) * 4 bytes) is rejected with
  * GNNC_ERR_UNSUPPORTED before anything is launched.
- * The first call on a device looks up the array's device address (once per
- * device, that device current); make that first call before any stream
- * capture. All calls on a device share the one array: calls that overlap on
- * the GPU (different streams or contexts of the same device) race and give
- * wrong results; serialise them. */
+ * gnnc_init looks up the array's device address for its context (that device
+ * current). With CUDA's lazy module loading that lookup is what loads this
+ * library's device code on the device and reserves the 16 MiB, so any
+ * allocation happens in gnnc_init and never in this entry point. The address
+ * belongs to the context: after cudaDeviceReset (which also frees the
+ * context's own buffers) make a new context. All calls on a device share the
+ * one array, which keeps the last call's contents (the counters are cleared
+ * by each call): calls that overlap on the GPU (different streams or contexts
+ * of the same device) race and give wrong results; serialise them. */
 GNNC_API int gnnc_gat_aggregate_noalloc(gnnc_ctx_t* ctx, const gnnc_plan_t* plan,
                                         const int32_t* rowptr, const int32_t* col, const void* h,
                                         int h_dtype, int64_t ldh, const float* asrc,

@@ -32,7 +32,6 @@
 //  * Epilogue, fused: divide by the softmax denominator, concat or mean over
 //    heads, + bias, ReLU / ELU, optional row log_softmax, convert, store.
 #include <algorithm>
-#include <mutex>
 #include <vector>
 
 #include "common.cuh"
@@ -1626,7 +1625,10 @@ extern "C" int gnnc_softmax_aggregate(gnnc_ctx_t* ctx, const gnnc_plan_t* plan,
 // has seen before; gnnc_gat_aggregate_noalloc never allocates. Its scratch -
 // the scheduling counters, the bad-index flag and the split-row partials -
 // lives in the fixed array below, which every GPU that loads this library
-// holds until the process exits.
+// holds until the process exits. gnnc_init looks up the array's device
+// address for its context (with lazy module loading that lookup is what loads
+// this library's device code on the device and reserves the array), so no
+// call of the entry point itself allocates.
 
 namespace {
 
@@ -1635,26 +1637,6 @@ constexpr size_t kStaticCounterBytes = 256;               // counters first, par
 
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
-std::mutex g_static_mu;
-void* g_static_addr[256] = {};  // device address of g_static_scratch, per device
-
-// Looks up (once per device, with that device current) the device address of
-// g_static_scratch. In host code the array's name is only a host-side stand-in,
-// so kernels get this address instead.
-int static_scratch(gnnc_ctx_t* ctx, unsigned char** out) {
-  std::lock_guard<std::mutex> lock(g_static_mu);
-  if (ctx->device < 0 || ctx->device >= 256)
-    return gnnc::set_error(ctx, GNNC_ERR_UNSUPPORTED, "device index %d out of range", ctx->device);
-  if (!g_static_addr[ctx->device]) {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
-    if (e != cudaSuccess) return gnnc::cuda_status(ctx, e, "cudaGetSymbolAddress(static scratch)");
-    g_static_addr[ctx->device] = p;
-  }
-  *out = reinterpret_cast<unsigned char*>(g_static_addr[ctx->device]);
-  return GNNC_OK;
-}
-
 // ORs the call's bad-index flag into the context's flag word, which
 // gnnc_synchronize reports.
 __global__ void fold_flag_kernel(const int* from, int* into) {
@@ -1662,6 +1644,17 @@ __global__ void fold_flag_kernel(const int* from, int* into) {
 }
 
 }  // namespace
+
+namespace gnnc {
+
+cudaError_t resolve_static_scratch(gnnc_ctx_t* ctx) {
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+  ctx->static_scratch = e == cudaSuccess ? p : nullptr;
+  return e;
+}
+
+}  // namespace gnnc
 
 extern "C" int gnnc_gat_aggregate_noalloc(gnnc_ctx_t* ctx, const gnnc_plan_t* plan,
                                           const int32_t* rowptr, const int32_t* col,
@@ -1682,9 +1675,11 @@ extern "C" int gnnc_gat_aggregate_noalloc(gnnc_ctx_t* ctx, const gnnc_plan_t* pl
   if (n_rows == 0) return GNNC_OK;
   GNNC_CHECK_ARG(ctx, asrc && adst, "null attention coefficients");
   GNNC_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
-  unsigned char* scratch = nullptr;
-  st = static_scratch(ctx, &scratch);
-  if (st) return st;
+  // The array's device address, looked up once by gnnc_init. In host code the
+  // name g_static_scratch is only a host-side stand-in, never passed to a kernel.
+  unsigned char* scratch = reinterpret_cast<unsigned char*>(ctx->static_scratch);
+  if (!scratch)
+    return gnnc::set_error(ctx, GNNC_ERR_CUDA, "fixed scratch address was not resolved");
 
   AggParams p = base_params(plan);
   p.rowptr = rowptr; p.col = col; p.scores = nullptr; p.asrc = asrc; p.adst = adst;

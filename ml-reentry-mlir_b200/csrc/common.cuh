@@ -23,6 +23,9 @@ struct gnnc_ctx {
   bool ws_owned = true;
   // Small device area: [0..7] scheduling counters, [8..15] result/error words.
   int* dev_words = nullptr;
+  // Device address of the fixed scratch array of gnnc_gat_aggregate_noalloc,
+  // looked up by gnnc_init with the device current (aggregate.cu).
+  void* static_scratch = nullptr;
   // NCCL communicator (ncclComm_t) of gnnc_comm_init, or null.
   void* comm = nullptr;
   int comm_rank = 0;
@@ -61,6 +64,10 @@ int set_error(gnnc_ctx_t* ctx, int status, const char* fmt, ...);
 
 // Destroys the context's communicator, if any (comm.cu).
 void comm_release(gnnc_ctx_t* ctx);
+
+// Sets ctx->static_scratch to the device address of the no-alloc entry
+// point's fixed array; the device must be current (aggregate.cu).
+cudaError_t resolve_static_scratch(gnnc_ctx_t* ctx);
 
 // Returns GNNC_ERR_CUDA with text if err != cudaSuccess.
 int cuda_status(gnnc_ctx_t* ctx, cudaError_t err, const char* what);

@@ -71,11 +71,15 @@ int gnnc_init(int device, gnnc_ctx_t** out_ctx) {
   gnnc_ctx_t* ctx = new (std::nothrow) gnnc_ctx_t();
   if (!ctx) return GNNC_ERR_OOM;
   ctx->device = device;
+  // The fixed scratch of gnnc_gat_aggregate_noalloc is resolved here, so that
+  // the module load and the array's reservation happen at set-up, not inside
+  // that entry point.
   if (cudaSetDevice(device) != cudaSuccess ||
       cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device) !=
           cudaSuccess ||
       cudaMalloc(&ctx->dev_words, 64 * sizeof(int)) != cudaSuccess ||
-      cudaMemset(ctx->dev_words, 0, 64 * sizeof(int)) != cudaSuccess) {
+      cudaMemset(ctx->dev_words, 0, 64 * sizeof(int)) != cudaSuccess ||
+      gnnc::resolve_static_scratch(ctx) != cudaSuccess) {
     if (ctx->dev_words) cudaFree(ctx->dev_words);
     delete ctx;
     return GNNC_ERR_CUDA;

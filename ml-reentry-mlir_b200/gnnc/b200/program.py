@@ -475,11 +475,13 @@ class B200Executable:
     host_chunk_min_edges = 1 << 21
 
     def run_device(self, x: torch.Tensor, graph: torch.Tensor, events: list | None = None,
-                   host_out=None) -> torch.Tensor:
+                   host_out=None, layer_outputs: list | None = None) -> torch.Tensor:
         """Forward on device-resident (or host) inputs; returns the device output.
 
         events: if a list, receives per layer a (projection_start, aggregation_start,
         end) triple of recorded CUDA events (for per-layer timing).
+        layer_outputs: if a list, receives each layer's device output rows in
+        order (the last one is the result).
         host_out: if given, a callable (shape, dtype) -> page-locked host tensor;
         the result is copied into it (overlapped with the last aggregation) and
         the host tensor is returned once the copies are queued (synchronize the
@@ -524,6 +526,8 @@ class B200Executable:
                 else:
                     self._aggregate(layer, g, g.plan, 0, n, h, asrc, adst, bias, out, root)
                     h_in = out
+                if layer_outputs is not None:
+                    layer_outputs.append(out)
                 if ev:
                     ev[2].record()
         return h_in

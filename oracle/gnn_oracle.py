@@ -20,6 +20,8 @@ plain PyTorch CPU ops, following the reference's own call sites:
   softmax_aggregate     <- experiments/gat-gpu-codegen/gat-kernel.mlir:31-132
   gat_rows_fp64         <- the same GAT math, chunked over destination rows in
                            float64 for graphs whose E x H x C messages do not fit
+  gat_layer_sample /    <- the same op sequence on a row range, the timed CPU
+  gat_aggregate_sample     baseline (with / without the projection)
   spmm_mean / sage_layer <- test/reference/sage.raw.mlir:5-27 and the mean rewrite
                            gnnc/conversion/tm_tensor_to_torch/despecialize_sparse_mm_reduce.py:1-75
 
@@ -311,6 +313,28 @@ def gat_layer_sample(x_rows, weight, att_src, att_dst, bias, heads, channels, h_
     if bias is not None:
         out = out + bias
     return F.elu(out)
+
+
+def gat_aggregate_sample(rowptr, col, h_src, asrc_src, adst_rows, heads, negative_slope=0.2):
+    """The CPU-baseline sample of the fused chain alone (given h, a_src,
+    a_dst; no projection, bias or activation): PyG's op sequence for the
+    destination rows [0, R), R = len(adst_rows), over the edges
+    col[:rowptr[R]] (gat.1-raw-torch.mlir:25-125)."""
+    H = heads
+    R = adst_rows.size(0)
+    C = h_src.size(1) // H
+    e_r = int(rowptr[R])
+    src = torch.as_tensor(col[:e_r], dtype=torch.int64)
+    dst = torch.repeat_interleave(torch.arange(R), torch.as_tensor(rowptr[: R + 1]).diff())
+    e = F.leaky_relu(asrc_src.index_select(0, src) + adst_rows.index_select(0, dst), negative_slope)
+    idx = dst.view(-1, 1).expand_as(e)
+    m = e.new_zeros((R, H)).scatter_reduce(0, idx, e, "amax", include_self=False)
+    p = (e - m.index_select(0, dst)).exp()
+    s = e.new_zeros((R, H)).scatter_add(0, idx, p) + 1e-16
+    alpha = p / s.index_select(0, dst)
+    msg = alpha.unsqueeze(-1) * h_src.view(-1, H, C).index_select(0, src)
+    out = h_src.new_zeros((R, H, C)).scatter_add(0, dst.view(-1, 1, 1).expand_as(msg), msg)
+    return out.view(-1, H * C)
 
 
 def gcn_rows_fp64(rowptr, col, w, h, *, rows=None, bias=None, act=None, log_softmax=False):

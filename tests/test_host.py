@@ -175,15 +175,26 @@ def test_graph_cache_key_survives_detach_and_tracks_updates():
     assert B200Executable._graph_key(other) != B200Executable._graph_key(ei)
 
 
-def test_bench_rejects_read_modes_of_another_exchange():
-    """bench.py: --peer-read gather belongs to the needed-rows exchange and tma
-    to the peer exchange; other pairings stop at argument parsing."""
-    import subprocess
+def test_bench_roofline_uses_dram_bytes_of_the_current_kernel_only(tmp_path, monkeypatch):
+    """bench.py's roofline: the primary figure is the ncu DRAM traffic of a
+    capture whose recorded kernel-source hash matches the current source (one
+    GPU only); otherwise the edge-gather model, labelled as an upper count."""
+    import importlib
     import sys
 
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    for args, msg in ((["--peer-read", "gather"], "goes with --exchange needed"),
-                      (["--exchange", "needed", "--peer-read", "tma"], "goes with --exchange peer")):
-        res = subprocess.run([sys.executable, os.path.join(root, "bench.py"), *args],
-                             capture_output=True, text=True, timeout=300)
-        assert res.returncode == 2 and msg in res.stderr, res.stderr[-500:]
+    sys.path.insert(0, root)
+    bench = importlib.import_module("bench")
+    prof = tmp_path / "prof.txt"
+    monkeypatch.setitem(bench.TRAFFIC_FILES, bench.WORKLOAD, prof)
+    cur = bench.kernel_source_hash()
+    prof.write_text(f"dram_bytes_per_launch_full_size: 20.0e9 bytes\nkernel_source_sha256_16: {cur}\n")
+    r = bench.roofline("k", bench.WORKLOAD, 35.0e9, 4.0, 1)
+    assert r["basis"] == "dram" and r["traffic"] == 20_000_000_000
+    assert abs(r["achieved"] - 20.0e9 / 4e-3 / 1e9) < 1e-6 and r["frac"] == r["frac_dram"]
+    assert r["algorithmic"]["achieved"] > r["achieved"]
+    r2 = bench.roofline("k", bench.WORKLOAD, 35.0e9, 4.0, 2)  # a rank's share: not that capture
+    assert r2["traffic"] is None and r2["frac_dram"] is None and r2["basis"].startswith("edge-gather")
+    prof.write_text("dram_bytes_per_launch_full_size: 20.0e9 bytes\nkernel_source_sha256_16: 0000\n")
+    r3 = bench.roofline("k", bench.WORKLOAD, 35.0e9, 4.0, 1)  # stale capture
+    assert r3["traffic"] is None and not r3["traffic_source"]["current"]

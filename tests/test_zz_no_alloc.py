@@ -54,6 +54,39 @@ def test_noalloc_matches_allocating_entry_point_twice(device, dtype, out_dtype):
         assert_close(out, ref, rtol=tol, atol=tol)
 
 
+def test_noalloc_leaves_free_device_memory_unchanged(device):
+    """The claim itself: with a plan that has more split-row segments than
+    any call before it (the allocating entry point would grow its workspace),
+    two calls leave the device's free memory exactly where it was."""
+    from gnnc.b200 import runtime as rt
+
+    n, H, C = 5000, 4, 64
+    h = rt.empty_rows(n, H * C, torch.bfloat16, device)
+    h.normal_()
+    asrc = torch.randn(n, H, device=device)
+    adst = torch.randn(n, H, device=device)
+    outs = [rt.empty_rows(n, H * C, torch.bfloat16, device) for _ in range(2)]
+    # warm-up on a small plan with split rows: the kernels of this layout are
+    # loaded (loading a kernel may reserve device memory) by both entry points
+    rp_s, col_s, plan_s = _graph(device, 1000, 8000, heavy=((1, 3000),), cta=32, split=512)
+    assert plan_s.info()["n_split_rows"] >= 1
+    rt.gat_aggregate_noalloc(plan_s, rp_s, col_s, h, asrc, adst[:1000], outs[0][:1000], heads=H)
+    rt.gat_aggregate(plan_s, rp_s, col_s, h, asrc, adst[:1000], heads=H, out_dtype=torch.bfloat16)
+    rowptr, col, plan = _graph(device, n, 80000, heavy=((2, 30000), (8, 25000), (13, 9000)),
+                               cta=32, split=64)
+    info = plan.info()
+    assert info["n_segments"] >= 900 > 8 * plan_s.info()["n_segments"]
+    torch.cuda.synchronize(device)
+    free_before = torch.cuda.mem_get_info(device)[0]
+    for out in outs:
+        rt.gat_aggregate_noalloc(plan, rowptr, col, h, asrc, adst, out, heads=H)
+    rt.Context.get(device).synchronize()
+    assert torch.cuda.mem_get_info(device)[0] == free_before
+    ref = rt.gat_aggregate(plan, rowptr, col, h, asrc, adst, heads=H, out_dtype=torch.bfloat16)
+    assert_close(outs[0], ref, rtol=2e-2, atol=2e-2)
+    assert torch.equal(outs[0], outs[1])
+
+
 def test_noalloc_mean_heads_log_softmax(device):
     from gnnc.b200 import runtime as rt
 
