@@ -313,6 +313,16 @@ GNNC_API int gnnc_gather_rows(gnnc_ctx_t* ctx, const void* src, int64_t ld_src,
                               const int32_t* idx, int64_t n, int64_t n_src, void* dst,
                               int64_t ld_dst, int64_t row_bytes);
 
+/* Diagnostics; no counterpart in the reference. Every wait of the tensor-core
+ * projection on its pipeline (mbarriers) gives up after 2 s of %globaltimer,
+ * raises an abort flag, drains its copies / MMAs and frees TMEM, and
+ * gnnc_synchronize then returns GNNC_ERR_TIMEOUT. gnnc_wait_selftest runs that
+ * same bounded wait on an mbarrier that nothing arrives on (nothing else in
+ * flight), with a limit of limit_ns (0 < limit_ns <= 2e9), on ctx's stream:
+ * the next gnnc_synchronize returns GNNC_ERR_TIMEOUT and clears the report,
+ * and the context stays usable. */
+GNNC_API int gnnc_wait_selftest(gnnc_ctx_t* ctx, int64_t limit_ns);
+
 /* One NCCL communicator per context, for the exchange step of a
  * destination-row partition (replaces the reference-side all-gather a
  * partitioned layer needs; the reference itself has no multi-GPU path,
@@ -320,19 +330,33 @@ GNNC_API int gnnc_gather_rows(gnnc_ctx_t* ctx, const void* src, int64_t ld_src,
  *   gnnc_comm_unique_id : rank 0 makes the id (GNNC_COMM_ID_BYTES bytes) and
  *                         hands it to the other ranks by any host means
  *   gnnc_comm_init      : joins communicator `id` as `rank` of `nranks` on
- *                         ctx's device (blocks until every rank has joined)
+ *                         ctx's device, waiting at most 120 s for every rank
+ *   gnnc_comm_init_timeout : the same with a deadline of timeout_ms: if not
+ *                         every rank has joined by then, the communicator is
+ *                         aborted and GNNC_ERR_TIMEOUT returned (the context
+ *                         stays usable and may join another communicator)
  *   gnnc_allgather      : recvbuf[r*count .. (r+1)*count) = rank r's sendbuf
  *                         (count elements of dtype GNNC_F32 or GNNC_BF16), on
  *                         ctx's stream
+ *   gnnc_comm_wait      : waits at most timeout_ms for ctx's stream (its
+ *                         collectives included); a collective that cannot
+ *                         finish (a peer died between steps) aborts the
+ *                         communicator and returns GNNC_ERR_TIMEOUT, an
+ *                         asynchronous NCCL error returns GNNC_ERR_NCCL
  *   gnnc_comm_destroy   : waits for ctx's stream, destroys the communicator
  *                         (gnnc_destroy also does)
- * NCCL is loaded on first use (the copy already in the process, else
- * libnccl.so.2); failures return GNNC_ERR_NCCL with NCCL's message. */
+ * Communicators are non-blocking (ncclConfig_t.blocking = 0): the host polls
+ * their state against the deadlines instead of blocking inside NCCL. NCCL is
+ * loaded on first use (the copy already in the process, else libnccl.so.2);
+ * failures return GNNC_ERR_NCCL with NCCL's message. */
 #define GNNC_COMM_ID_BYTES 128
 GNNC_API int gnnc_comm_unique_id(gnnc_ctx_t* ctx, void* id);
 GNNC_API int gnnc_comm_init(gnnc_ctx_t* ctx, const void* id, int rank, int nranks);
+GNNC_API int gnnc_comm_init_timeout(gnnc_ctx_t* ctx, const void* id, int rank, int nranks,
+                                    int64_t timeout_ms);
 GNNC_API int gnnc_allgather(gnnc_ctx_t* ctx, const void* sendbuf, void* recvbuf, size_t count,
                             int dtype);
+GNNC_API int gnnc_comm_wait(gnnc_ctx_t* ctx, int64_t timeout_ms);
 GNNC_API int gnnc_comm_destroy(gnnc_ctx_t* ctx);
 
 #ifdef __cplusplus

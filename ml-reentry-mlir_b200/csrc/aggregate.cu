@@ -116,11 +116,28 @@ struct VecLoad<__nv_bfloat16, 1> {
   }
 };
 
-// ELU as expm1(x) for x <= 0, as torch's elu computes it: forming exp(x) - 1
-// would cancel for small |x| and lose the relative accuracy there.
+// expm1(v) for v <= 0 (ELU's negative branch, which torch computes as expm1).
+// exp(v) - 1 alone cancels for small |v|, so above -0.5 the Taylor series
+// sum_{k=1..7} v^k / k! is used (truncation error below v^7 / 7! relative,
+// < 2e-7 on (-0.5, 0]), evaluated by Horner's rule; below -0.5, exp(v) <= 0.61
+// and exp(v) - 1 keeps full relative accuracy.
+__device__ __forceinline__ float expm1_nonpos(float v) {
+  if (v > -0.5f) {
+    float p = 1.f / 5040.f;
+    p = fmaf(p, v, 1.f / 720.f);
+    p = fmaf(p, v, 1.f / 120.f);
+    p = fmaf(p, v, 1.f / 24.f);
+    p = fmaf(p, v, 1.f / 6.f);
+    p = fmaf(p, v, 0.5f);
+    p = fmaf(p, v, 1.f);
+    return v * p;
+  }
+  return __expf(v) - 1.f;
+}
+
 __device__ __forceinline__ float apply_act(float v, int act) {
   if (act == GNNC_ACT_RELU) return fmaxf(v, 0.f);
-  if (act == GNNC_ACT_ELU) return v > 0.f ? v : expm1f(v);
+  if (act == GNNC_ACT_ELU) return v > 0.f ? v : expm1_nonpos(v);
   return v;
 }
 
@@ -142,7 +159,8 @@ __device__ __forceinline__ float out_value(const AggParams& p, int64_t row, cons
 
 // Epilogue for one row, run by one full warp. s_row holds the aggregated
 // (already normalised) [F] values.
-__device__ void warp_epilogue(const AggParams& p, int64_t row, const float* s_row, int lane) {
+__device__ __forceinline__ void warp_epilogue(const AggParams& p, int64_t row, const float* s_row,
+                                              int lane) {
   const int Fo = p.F_out;
   if (Fo <= 64) {
     // At most two columns per lane: each output value is formed once and kept

@@ -128,8 +128,9 @@ int gnnc_synchronize(gnnc_ctx_t* ctx) {
   if (words[1]) {
     GNNC_CUDA_TRY(ctx, cudaMemset(ctx->dev_words + 3, 0, sizeof(int)));
     return gnnc::set_error(ctx, GNNC_ERR_TIMEOUT,
-                           "a tensor-core projection gave up waiting on its pipeline; "
-                           "its output is incomplete");
+                           "a bounded wait on the device gave up (a tensor-core projection "
+                           "waiting on its pipeline: its output is incomplete; or "
+                           "gnnc_wait_selftest)");
   }
   if (flag) {
     GNNC_CUDA_TRY(ctx, cudaMemset(ctx->dev_words + 2, 0, sizeof(int)));

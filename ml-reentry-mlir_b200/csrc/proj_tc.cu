@@ -118,15 +118,35 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
 // Waits for the phase `parity` of barrier b. Returns false when the wait gave
 // up (time limit) or another role aborted; a time-out raises the abort flag.
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort,
-                                          bool watch_abort = true) {
+                                          bool watch_abort = true,
+                                          unsigned long long limit_ns = kWaitNs) {
   const unsigned long long t0 = now_ns();
   for (;;) {
     if (mbar_try_wait(b, parity)) return true;
     if (watch_abort && *abort) return false;
-    if (now_ns() - t0 > kWaitNs) {
+    if (now_ns() - t0 > limit_ns) {
       *abort = 1;
       return false;
     }
+  }
+}
+
+// Self-test of the bounded wait and of its error report: thread 0 waits, with
+// the projection's mbar_wait, on an mbarrier that nothing ever arrives on.
+// The wait gives up after limit_ns and the kernel records GNNC_ERR_TIMEOUT in
+// the context's error word exactly as a projection whose wait gave up does.
+// Nothing is in flight (no copy, no MMA, no TMEM), so giving up is harmless.
+__global__ void wait_selftest_kernel(int* err, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    volatile int* abort = &abort_flag;
+    if (!mbar_wait(&bar, 0, abort, true, limit_ns) && *abort) atomicExch(err, GNNC_ERR_TIMEOUT);
   }
 }
 
@@ -703,3 +723,14 @@ int proj_tc_try(gnnc_ctx_t* ctx, const void* x, int64_t ldx, const void* w, int6
 }
 
 }  // namespace gnnc
+
+extern "C" int gnnc_wait_selftest(gnnc_ctx_t* ctx, int64_t limit_ns) {
+  if (!ctx) return GNNC_ERR_INVALID;
+  GNNC_CHECK_ARG(ctx, limit_ns > 0 && limit_ns <= int64_t(kWaitNs),
+                 "gnnc_wait_selftest: limit must be in (0, %llu] ns", kWaitNs);
+  GNNC_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  wait_selftest_kernel<<<1, 32, 0, ctx->stream>>>(ctx->dev_words + 3,
+                                                  (unsigned long long)limit_ns);
+  GNNC_CUDA_TRY(ctx, cudaGetLastError());
+  return GNNC_OK;
+}

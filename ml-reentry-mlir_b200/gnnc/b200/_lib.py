@@ -82,7 +82,10 @@ SIGNATURES: dict[str, tuple] = {
     "gnnc_gather_rows": (c_int, [_P, _P, _I64, _P, _I64, _I64, _P, _I64, _I64]),
     "gnnc_comm_unique_id": (c_int, [_P, _P]),
     "gnnc_comm_init": (c_int, [_P, _P, c_int, c_int]),
+    "gnnc_comm_init_timeout": (c_int, [_P, _P, c_int, c_int, _I64]),
     "gnnc_allgather": (c_int, [_P, _P, _P, c_size_t, c_int]),
+    "gnnc_comm_wait": (c_int, [_P, _I64]),
+    "gnnc_wait_selftest": (c_int, [_P, _I64]),
     "gnnc_comm_destroy": (c_int, [_P]),
     "gnnc_gat_aggregate_noalloc": (
         c_int,

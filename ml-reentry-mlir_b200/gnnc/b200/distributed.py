@@ -18,7 +18,8 @@ the narrower side of its projection:
 The layer's aggregation then reads local memory only and writes its rows
 straight into the next layer's input slot. A fence orders each exchanged
 buffer's writes before the peers' reads (a one-word NCCL all-reduce on the
-stream, or a host barrier for gloo process groups), and one more at the end of
+stream, or a host barrier for gloo process groups that names a rank which
+stopped arriving, `host_fence`), and one more at the end of
 the forward orders the last reads before the next forward's writes. The
 results are those of the single-GPU executable, row for row: every row is
 projected and aggregated by the same kernels on the same values.
@@ -27,12 +28,25 @@ projected and aggregated by the same kernels on the same values.
 from __future__ import annotations
 
 from dataclasses import dataclass
+from datetime import timedelta
 
 import torch
 
 from gnnc.b200 import partition as P
 from gnnc.b200 import runtime as rt
 from gnnc.b200.program import B200Executable
+
+
+def host_fence(group=None, timeout: timedelta = timedelta(seconds=60)) -> None:
+    """Host barrier over a gloo group that detects a rank that is gone.
+
+    torch.distributed.monitored_barrier: rank 0 waits for every other rank up
+    to `timeout`; a rank that died or stopped between steps makes the barrier
+    raise RuntimeError naming it (on rank 0; the others see their barrier
+    fail), instead of every rank waiting out the process group's own timeout."""
+    import torch.distributed as dist
+
+    dist.monitored_barrier(group=group, timeout=timeout, wait_all_ranks=True)
 
 
 @dataclass
@@ -94,11 +108,13 @@ class DistributedExecutable:
 
     PIECE_ROWS = 1 << 18
 
-    def __init__(self, exe: B200Executable, group=None, fence: str = "auto") -> None:
+    def __init__(self, exe: B200Executable, group=None, fence: str = "auto",
+                 fence_timeout: timedelta = timedelta(seconds=60)) -> None:
         import torch.distributed as dist
 
         self.exe, self.program, self.device = exe, exe.program, exe.device
         self.group = group
+        self.fence_timeout = fence_timeout
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         if fence == "auto":
@@ -122,7 +138,7 @@ class DistributedExecutable:
             dist.all_reduce(self._fence_buf, group=self.group)
         else:
             torch.cuda.synchronize(self.device)
-            dist.barrier(group=self.group)
+            host_fence(self.group, self.fence_timeout)
 
     def exchange_modes(self) -> list[str]:
         """Per layer, the side of the projection that crosses NVLink."""
@@ -305,11 +321,12 @@ class DistributedExecutable:
         return out.contiguous()
 
 
-def distribute(exe: B200Executable, group=None, fence: str = "auto") -> DistributedExecutable:
+def distribute(exe: B200Executable, group=None, fence: str = "auto",
+               fence_timeout: timedelta = timedelta(seconds=60)) -> DistributedExecutable:
     """Wraps a compiled executable for a row-partitioned forward over `group`."""
     if not isinstance(exe, B200Executable):
         raise NotImplementedError(f"cannot distribute {type(exe).__name__}")
-    return DistributedExecutable(exe, group=group, fence=fence)
+    return DistributedExecutable(exe, group=group, fence=fence, fence_timeout=fence_timeout)
 
 
-__all__ = ["DistributedExecutable", "distribute"]
+__all__ = ["DistributedExecutable", "distribute", "host_fence"]

@@ -655,12 +655,26 @@ def comm_unique_id(device: torch.device | int) -> bytes:
     return uid.raw
 
 
-def comm_init(device: torch.device | int, uid: bytes, rank: int, nranks: int) -> None:
-    """Joins communicator `uid` as `rank` of `nranks` (blocks until all have joined)."""
+def comm_init(device: torch.device | int, uid: bytes, rank: int, nranks: int,
+              timeout_ms: int | None = None) -> None:
+    """Joins communicator `uid` as `rank` of `nranks`. Waits at most timeout_ms
+    (default 120 s) for every rank; past it the communicator is aborted and a
+    GnncError with status ERR_TIMEOUT is raised (the context stays usable)."""
     if len(uid) != COMM_ID_BYTES:
         raise ValueError(f"communicator id must be {COMM_ID_BYTES} bytes")
     ctx = Context.get(device)
-    raise_for(ctx.lib.gnnc_comm_init(ctx.handle, uid, rank, nranks), ctx.handle, "gnnc_comm_init")
+    if timeout_ms is None:
+        st = ctx.lib.gnnc_comm_init(ctx.handle, uid, rank, nranks)
+    else:
+        st = ctx.lib.gnnc_comm_init_timeout(ctx.handle, uid, rank, nranks, int(timeout_ms))
+    raise_for(st, ctx.handle, "gnnc_comm_init")
+
+
+def comm_wait(device: torch.device | int, timeout_ms: int) -> None:
+    """Waits at most timeout_ms for the context's stream and its collectives; a
+    collective that cannot finish aborts the communicator (ERR_TIMEOUT)."""
+    ctx = Context.get(device)
+    raise_for(ctx.lib.gnnc_comm_wait(ctx.handle, int(timeout_ms)), ctx.handle, "gnnc_comm_wait")
 
 
 def allgather(send: torch.Tensor, recv: torch.Tensor) -> torch.Tensor:

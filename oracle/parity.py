@@ -181,17 +181,24 @@ def compare(got: torch.Tensor, ref: torch.Tensor, *, rtol: float, atol: float) -
 
 
 def argmax_agreement(got: torch.Tensor, ref: torch.Tensor, max_abs_err: float) -> dict:
-    """Class predictions of got vs ref. A row whose oracle top-2 margin is
-    within 2 x the observed max abs error can flip legitimately (a tie within
-    rounding); such rows are counted and excluded, every other row must agree."""
+    """Class predictions of got vs ref over the checked rows.
+
+    A prediction can differ only where the oracle's top-2 margin is at most
+    twice the error of the two entries, so rows with margin <= 2 x the
+    observed max abs error are near-ties (counted, not required to agree);
+    every other row must agree ("pass"). Also reported: how many rows differ
+    at all, and the largest oracle margin among them (how close the flips
+    were)."""
     top2 = ref.double().topk(2, dim=1).values
-    tie = (top2[:, 0] - top2[:, 1]) <= 2 * max_abs_err
-    a, b = got.argmax(1), ref.argmax(1)
-    differ = a != b
+    margin = top2[:, 0] - top2[:, 1]
+    tie = margin <= 2 * max_abs_err
+    differ = got.argmax(1) != ref.argmax(1)
     return {
         "pass": not bool((differ & ~tie).any()),
         "rows": int(got.size(0)),
+        "disagree": int(differ.sum()),
         "disagree_decided": int((differ & ~tie).sum()),
-        "near_ties_excluded": int(tie.sum()),
-        "disagree_among_ties": int((differ & tie).sum()),
+        "near_ties": int(tie.sum()),
+        "max_margin_of_disagreeing_rows": float(margin[differ].max()) if bool(differ.any()) else 0.0,
+        "median_margin": float(margin.median()),
     }

@@ -7,8 +7,10 @@ float64 layer computed from the same input the GPU layer read (the input X for
 layer 1, the previous GPU layer's bf16 output after that), on every row of
 in-degree > 1024 (the CTA-path hubs) plus 50,000 seeded rows. Tolerance 2e-2
 (bf16 features); the last layer's class predictions must agree on every
-checked row except near-ties within twice the observed max error, whose count
-is bounded. Reference semantics: experiments/gatconv/dumps/gat.1-raw-torch.mlir:5-129
+checked row except near-ties (oracle top-2 margin within twice the observed
+max error), and at most 1% of the checked rows may differ at all (random
+weights give near-uniform 47-class outputs, so bf16 rounding flips some
+near-ties; the count and the largest flipped margin are printed). Reference semantics: experiments/gatconv/dumps/gat.1-raw-torch.mlir:5-129
 (GATConv), gnnc/examples/models/gcn.py:32-51 and test/reference/gcn.raw.mlir:6-21
 (GCN stack)."""
 
@@ -24,7 +26,7 @@ pytestmark = pytest.mark.gpu
 TOL = 2e-2
 SAMPLE = 50_000
 HUB = 1024
-MAX_TIE_FRACTION = 0.01
+MAX_FLIP_FRACTION = 0.01
 
 
 def _forward(model_name, device):
@@ -53,8 +55,9 @@ def _check_layers(convs, x, outs, layer_rows_fn):
         assert res["pass"], f"layer {i + 1}: {res}"
         if last:
             arg = PY.argmax_agreement(got[rows].float(), ref, res["max_abs_err"])
+            print(f"layer {i + 1}: {res}\nargmax: {arg}")
             assert arg["pass"], f"last layer argmax: {arg}"
-            assert arg["near_ties_excluded"] <= MAX_TIE_FRACTION * arg["rows"], arg
+            assert arg["disagree"] <= MAX_FLIP_FRACTION * arg["rows"], arg
     return report
 
 

@@ -34,11 +34,61 @@ def test_one_rank_communicator(device):
             rt.comm_init(device, uid, 0, 1)
         for t in (x, torch.randn(333, 4, device=device)):
             out = rt.allgather(t, torch.empty_like(t))
-            rt.Context.get(device).synchronize()
+            rt.comm_wait(device, 10000)
             assert torch.equal(out, t)
     finally:
         rt.comm_destroy(device)
     rt.comm_destroy(device)  # no communicator left: a no-op
+
+
+_NEVER_JOINED = r"""
+import sys, time
+sys.path[:0] = [ROOT, ROOT + "/ml-reentry-mlir_b200"]
+import torch
+from gnnc.b200 import runtime as rt
+from gnnc.b200._lib import ERR_TIMEOUT, GnncError
+
+dev = torch.device("cuda", 0)
+uid = rt.comm_unique_id(dev)
+t0 = time.monotonic()
+try:
+    rt.comm_init(dev, uid, 0, 2, timeout_ms=3000)  # rank 1 never joins
+    print("JOINED")
+    sys.exit(1)
+except GnncError as exc:
+    waited = time.monotonic() - t0
+    assert exc.status == ERR_TIMEOUT, exc
+    print(f"TIMEOUT after {waited:.2f}s: {exc}")
+# the context stays usable: a new one-rank communicator and a collective
+rt.comm_init(dev, rt.comm_unique_id(dev), 0, 1, timeout_ms=30000)
+x = torch.randn(256, 64, device=dev)
+y = rt.allgather(x, torch.empty_like(x))
+rt.comm_wait(dev, 10000)
+assert torch.equal(x, y)
+rt.comm_destroy(dev)
+print(f"WAITED {waited:.3f}")
+"""
+
+
+@pytest.mark.timeout(240)
+def test_comm_init_gives_up_when_a_rank_never_joins(device):
+    """gnnc_comm_init_timeout: rank 0 of a two-rank communicator whose rank 1
+    never joins returns GNNC_ERR_TIMEOUT shortly after its 3 s deadline (the
+    non-blocking communicator is aborted), and the same context then joins a
+    one-rank communicator and runs a collective. A fresh process with NVLS off:
+    nothing runs on the GPU while the join is pending."""
+    import subprocess
+
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", CUDA_VISIBLE_DEVICES=str(device.index or 0))
+    code = f"ROOT = {ROOT!r}\n" + _NEVER_JOINED
+    t0 = time.monotonic()
+    res = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                         timeout=200)
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-3000:]
+    assert "TIMEOUT after" in res.stdout, res.stdout
+    waited = float(res.stdout.split("WAITED")[1].split()[0])
+    assert 3.0 <= waited < 15.0, waited
+    assert time.monotonic() - t0 < 200
 
 
 def _rank(rank, world, path, out_dir):

@@ -93,3 +93,35 @@ def test_tensor_core_projection_epilogue(device, n, k, f, heads, h_dtype):
     big = big.cpu()
     assert bool((big[:, f:] == sentinel).all()), "columns past f were written"
     assert bool((big[n:] == sentinel).all()), "rows past n were written"
+
+
+def test_bounded_wait_gives_up_and_the_context_recovers(device):
+    """The projection's bounded mbarrier wait, run on a barrier nothing arrives
+    on with a 1 ms limit (gnnc_wait_selftest): gnnc_synchronize reports
+    GNNC_ERR_TIMEOUT once, the report is cleared, and the next tensor-core
+    projection on the same context succeeds and is correct."""
+    import time
+
+    from gnnc.b200 import runtime as rt
+    from gnnc.b200._lib import ERR_TIMEOUT, GnncError
+
+    ctx = rt.Context.get(device)
+    t0 = time.monotonic()
+    ctx.call("gnnc_wait_selftest", 1_000_000)
+    with pytest.raises(GnncError) as exc:
+        ctx.synchronize()
+    assert exc.value.status == ERR_TIMEOUT and "bounded wait" in str(exc.value)
+    assert time.monotonic() - t0 < 5.0
+    ctx.synchronize()  # cleared
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(3000, 100, generator=g).to(torch.bfloat16)
+    w = (torch.randn(256, 100, generator=g) * 0.1).to(torch.bfloat16)
+    xd = rt.empty_rows(3000, 100, torch.bfloat16, device)
+    xd.copy_(x)
+    wd = rt.empty_rows(256, 100, torch.bfloat16, device)
+    wd.copy_(w)
+    h = rt.proj(xd, wd, out_dtype=torch.float32)
+    ctx.synchronize()
+    assert_close(h, x.double() @ w.double().t(), rtol=1e-4, atol=1e-4)
+    with pytest.raises(ValueError):
+        ctx.call("gnnc_wait_selftest", 0)

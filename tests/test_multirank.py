@@ -244,3 +244,40 @@ def test_whole_graph_split_threshold_formula():
     assert P.whole_graph_split_threshold(64_308_169, 148) == 64_308_169 // 1184
     assert P.whole_graph_split_threshold(1000, 148) == 4096
     assert P.whole_graph_split_threshold(1 << 45, 148) == 1 << 30
+
+
+def _fence_rank(rank, world, port, out_dir):
+    sys.path[:0] = [ROOT, os.path.join(ROOT, "ml-reentry-mlir_b200")]
+    import time
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from gnnc.b200.distributed import host_fence
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=timedelta(seconds=60))
+    host_fence(timeout=timedelta(seconds=20))  # step 1: every rank arrives
+    if rank == 1:
+        time.sleep(12)  # stops between steps: never reaches the second fence
+        return
+    t0 = time.monotonic()
+    try:
+        host_fence(timeout=timedelta(seconds=2))
+        msg = "PASSED"
+    except RuntimeError as exc:
+        msg = f"RAISED {exc}"
+    with open(os.path.join(out_dir, "fence.txt"), "w") as f:
+        f.write(f"{time.monotonic() - t0:.3f}\n{msg}\n")
+
+
+def test_host_fence_names_a_rank_that_stopped_arriving(tmp_path):
+    """A rank that stops between steps: the next host fence raises on rank 0
+    within its 2 s bound, naming rank 1, instead of waiting out the process
+    group's 60 s timeout (gloo, two processes, no GPU)."""
+    import torch.multiprocessing as mp
+
+    mp.spawn(_fence_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    waited, msg = (tmp_path / "fence.txt").read_text().splitlines()[:2]
+    assert msg.startswith("RAISED") and "1" in msg, msg
+    assert 1.5 <= float(waited) < 10.0, waited

@@ -68,7 +68,8 @@ def test_compare_and_argmax_verdicts():
     c = P.compare(got, ref, rtol=2e-2, atol=2e-2)
     assert c["pass"] and abs(c["max_abs_err"] - 0.01) < 1e-12
     a = P.argmax_agreement(got, ref, c["max_abs_err"])
-    assert a["pass"] and a["near_ties_excluded"] == 1 and a["disagree_among_ties"] == 1
+    assert a["pass"] and a["near_ties"] == 1 and a["disagree"] == 1
+    assert abs(a["max_margin_of_disagreeing_rows"] - 0.01) < 1e-12
     got[0, 1] = 1.2  # a decided row flips
     assert not P.compare(got, ref, rtol=2e-2, atol=2e-2)["pass"]
     assert not P.argmax_agreement(got, ref, 0.01)["pass"]
