@@ -70,6 +70,8 @@ struct AggParams {
   const int4* split_rows;
   const int32_t* warp_tasks;
   int64_t n_warp_tasks;
+  const int2* stream_tasks;  // row ranges [x, y) of warp rows only (wide launches)
+  int64_t n_stream_tasks;
   int cta_threshold;
   float* partials;
   int part_stride;
@@ -575,6 +577,321 @@ struct AggFast {
   }
 };
 
+// ---------------------------------------------------------------------------
+// Prefetched edge stream for the 256-wide bf16 layout (AggFast's lane layout).
+//
+// Each edge's column index and a_src row (GCN: its weight) used to be loaded
+// at the head of the edge's 32-edge chunk, so a row paid three dependent
+// memory round trips (col, then a_src, then the h rows) before its first
+// FMA. Here a warp walks a contiguous edge range - a task of whole rows, or
+// its share of one long row - in 32-edge windows and stages them in shared
+// memory with asynchronous copies (cp.async) ahead of use: window w+3's
+// column indices and window w+2's a_src rows are in flight while a chunk that
+// starts in window w (and may end in w+1) is processed. Rows then start with
+// their inputs in shared memory and only the h gathers stay on the critical
+// path. Chunks are still counted from each row's first edge, so the
+// arithmetic and summation order per row are those of AggFast::range: results
+// do not depend on how rows are grouped into tasks.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+template <int KH>
+struct AggStream {
+  static constexpr int KA = KH == 0 ? 1 : KH;  // floats staged per edge (a_src row or weight)
+  static constexpr int HS = KH == 0 ? 1 : (KH | 1);
+
+  // Per-warp shared memory. Window slots are rings indexed by window & 3.
+  struct Win {
+    float as[4][32 * KA];    // a_src rows (GCN: weights) of windows w .. w+2
+    float adst[2][32 * KA];  // a_dst rows of the current / next batch of 31 rows
+    int32_t col[4][32];      // column indices of windows w .. w+3
+    int32_t rp[2][32];       // row pointers of the current / next batch of 31 rows
+  };
+
+  // The stream [s0, s1) and the current window (edges base .. base+32).
+  struct Cursor {
+    int s0, s1, w, base;
+    int epoch;  // counts the waits for all outstanding copies
+  };
+
+  static __device__ __forceinline__ void issue_col(const AggParams& p, Win& s, const Cursor& c,
+                                                   int w, int lane) {
+    const int k = c.s0 + 32 * w + lane;
+    if (k < c.s1) cp_async4(&s.col[w & 3][lane], p.col + k);
+  }
+
+  // Needs window w's column indices in shared memory.
+  static __device__ __forceinline__ void issue_as(const AggParams& p, Win& s, const Cursor& c,
+                                                  int w, int lane) {
+    const int k = c.s0 + 32 * w + lane;
+    if (k >= c.s1) return;
+    float* dst = &s.as[w & 3][lane * KA];
+    if constexpr (KH == 0) {
+      cp_async4(dst, p.w + k);
+    } else {
+      const int src = s.col[w & 3][lane];
+      if (unsigned(src) >= unsigned(p.n_src)) return;  // reported when the edge is processed
+      const float* a = p.asrc + size_t(src) * KH;
+      if constexpr (KH == 1) {
+        cp_async4(dst, a);
+      } else if constexpr (KH == 2) {
+        cp_async8(dst, a);
+      } else if constexpr (KH == 4) {
+        cp_async16(dst, a);
+      } else {
+        cp_async16(dst, a);
+        cp_async16(dst + 4, a + 4);
+      }
+    }
+  }
+
+  // Starts the stream [s0, s1) at window 0.
+  static __device__ __forceinline__ void begin(const AggParams& p, Win& s, Cursor& c, int s0,
+                                               int s1, int lane) {
+    c.s0 = s0;
+    c.s1 = s1;
+    c.epoch = 0;
+    for (int w = 0; w < 3; ++w) issue_col(p, s, c, w, lane);
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncwarp();
+    issue_as(p, s, c, 0, lane);
+    issue_as(p, s, c, 1, lane);
+    cp_async_commit();
+    advance_to(p, s, c, 0, lane);
+  }
+
+  // Window w becomes current. Once this returns, the column indices of
+  // windows w .. w+2 and the a_src rows of windows w, w+1 are in shared
+  // memory, and window w+2's a_src rows and window w+3's column indices are
+  // in flight. A 32-edge chunk that starts in window w ends in w or w+1.
+  static __device__ __forceinline__ void advance_to(const AggParams& p, Win& s, Cursor& c, int w,
+                                                    int lane) {
+    cp_async_wait_all();
+    ++c.epoch;
+    __syncwarp();
+    c.w = w;
+    c.base = c.s0 + 32 * w;
+    issue_as(p, s, c, w + 2, lane);
+    issue_col(p, s, c, w + 3, lane);
+    cp_async_commit();
+  }
+
+  // Accumulates the row's edges [eb, ee), which must be the next edges of
+  // the stream, in 32-edge chunks counted from eb. ad_reg: lane hd holds
+  // a_dst of head hd. Same arithmetic and order as AggFast<KH>::range.
+  static __device__ __forceinline__ void row(const AggParams& p, Win& s, Cursor& c, int eb,
+                                             int ee, float ad_reg, float (&acc)[8], float& s_acc,
+                                             float& m_reg, int32_t* s_col, float* s_p, int hv,
+                                             int lane) {
+    const char* hlane = reinterpret_cast<const char*>(p.h) + lane * 16;
+    const uint32_t ldh_b = uint32_t(p.ldh) * 2u;
+    const float* s_ph = s_p + hv;
+    float sc_reg = 1.f;
+    for (int cb = eb; cb < ee; cb += 32) {
+      if (cb >= c.base + 32) advance_to(p, s, c, c.w + 1, lane);
+      const int k = cb + lane;
+      bool valid = k < ee;
+      const int off = k - c.base;  // < 64 for every valid lane
+      const int slot = (c.w + (off >> 5)) & 3, pos = off & 31;
+      int src = valid ? s.col[slot][pos] : 0;
+      if (valid && unsigned(src) >= unsigned(p.n_src)) {
+        atomicOr(p.counters + 2, 1);
+        valid = false;
+        src = 0;
+      }
+      s_col[lane] = src;
+      const float* xs = &s.as[valid ? slot : 0][(valid ? pos : 0) * KA];
+      if constexpr (KH == 0) {
+        s_p[lane] = valid ? xs[0] : 0.f;
+      } else {
+        float x[KH];
+        if constexpr (KH == 4) {
+          const float4 v = *reinterpret_cast<const float4*>(xs);
+          x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+        } else if constexpr (KH == 2) {
+          const float2 v = *reinterpret_cast<const float2*>(xs);
+          x[0] = v.x; x[1] = v.y;
+        } else {
+#pragma unroll
+          for (int hd = 0; hd < KH; ++hd) x[hd] = xs[hd];
+        }
+        bool rescale = false;
+#pragma unroll
+        for (int hd = 0; hd < KH; ++hd) {
+          // every lane takes part in the shuffles and the reduction
+          const float ad = __shfl_sync(kFull, ad_reg, hd);
+          float e = -INFINITY;
+          if (valid) {
+            const float t = x[hd] + ad;
+            e = t > 0.f ? t : t * p.slope;
+          }
+          const float cmax = warp_max_redux(e);
+          const float m_old = __shfl_sync(kFull, m_reg, hd);
+          const float m_new = fmaxf(m_old, cmax);
+          const float pr = valid ? __expf(e - m_new) : 0.f;
+          const float sc = __expf(m_old - m_new);
+          if (lane == hd) {
+            sc_reg = sc;
+            m_reg = m_new;
+          }
+          rescale |= (cb != eb) && (m_new != m_old);
+          s_p[lane * HS + hd] = pr;
+        }
+        if (rescale) {  // warp-uniform
+          const float sc = __shfl_sync(kFull, sc_reg, hv);
+          s_acc *= sc;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] *= sc;
+        }
+      }
+      __syncwarp();
+      const int n = min(32, ee - cb);
+      int j = 0;
+      for (; j + 8 <= n; j += 8) {
+        const int32_t* cj = s_col + j;
+        const float* pj = s_ph + j * HS;
+        uint4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          v[u] = __ldg(reinterpret_cast<const uint4*>(hlane + size_t(uint32_t(cj[u])) * ldh_b));
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float a = pj[u * HS];
+          s_acc += a;
+          AggFast<KH>::fma_row(acc, a, v[u]);
+        }
+      }
+      for (; j < n; ++j) {
+        const uint4 v =
+            __ldg(reinterpret_cast<const uint4*>(hlane + size_t(uint32_t(s_col[j])) * ldh_b));
+        const float a = s_ph[j * HS];
+        s_acc += a;
+        AggFast<KH>::fma_row(acc, a, v);
+      }
+      __syncwarp();
+    }
+  }
+};
+
+// Phase 2 with the prefetched stream: a warp takes a task of consecutive warp
+// rows (the plan leaves the CTA rows out of these tasks, so the task's edges
+// are one contiguous range) and streams through its edges. The row pointers
+// and a_dst rows of the next 31 rows are staged the same way, one batch ahead.
+template <int KH>
+__device__ __forceinline__ void stream_tasks(const AggParams& p, typename AggStream<KH>::Win& s,
+                                             int32_t* s_col, float* s_p, float* s_row, int hv,
+                                             int lane) {
+  using S = AggStream<KH>;
+  using A = Agg<__nv_bfloat16, 8, 32, 1>;
+  constexpr int KA = S::KA;
+  const bool softmax = p.mode != MODE_GCN;
+  for (;;) {
+    int t = 0;
+    if (lane == 0) t = atomicAdd(p.counters + 1, 1);
+    t = __shfl_sync(kFull, t, 0);
+    if (t >= p.n_stream_tasks) break;
+    const int2 task = p.stream_tasks[t];
+    const int r0 = task.x, r1 = task.y;
+    int rr = 0;
+    if (lane < 2) rr = __ldg(p.rowptr + (lane == 0 ? r0 : r1));
+    const int s0 = int(max(int64_t(__shfl_sync(kFull, rr, 0)), p.e_lo));
+    const int s1 = int(min(int64_t(__shfl_sync(kFull, rr, 1)), p.e_hi));
+    // Row pointers rowptr[rb .. rb+31] and the a_dst rows of rows rb .. rb+30
+    // of one batch, into batch slot `slot`.
+    auto issue_batch = [&](int slot, int rb) {
+      const int nr = min(31, r1 - rb);
+      if (lane <= nr) cp_async4(&s.rp[slot][lane], p.rowptr + rb + lane);
+      if constexpr (KH > 0) {
+        if (lane < nr) {
+          const float* a = p.adst + size_t(rb + lane) * KH;
+          float* d = &s.adst[slot][lane * KA];
+          if constexpr (KH == 1) {
+            cp_async4(d, a);
+          } else if constexpr (KH == 2) {
+            cp_async8(d, a);
+          } else if constexpr (KH == 4) {
+            cp_async16(d, a);
+          } else {
+            cp_async16(d, a);
+            cp_async16(d + 4, a + 4);
+          }
+        }
+      }
+    };
+    issue_batch(0, r0);
+    cp_async_commit();
+    typename S::Cursor c;
+    S::begin(p, s, c, s0, s1, lane);  // its waits also land batch 0
+    int batch_epoch = c.epoch;
+    bool fresh = true;  // batch 0 landed in begin()
+    for (int rb = r0, bi = 0; rb < r1; rb += 31, bi ^= 1) {
+      if (!fresh && c.epoch == batch_epoch) {  // no window wait since it was issued
+        cp_async_wait_all();
+        ++c.epoch;
+        __syncwarp();
+      }
+      fresh = false;
+      if (rb + 31 < r1) {
+        issue_batch(bi ^ 1, rb + 31);
+        cp_async_commit();
+        batch_epoch = c.epoch;
+      }
+      const int nr = min(31, r1 - rb);
+      const int rpv = s.rp[bi][lane];
+      for (int i = 0; i < nr; ++i) {
+        const int r = rb + i;
+        const int eb = int(max(int64_t(__shfl_sync(kFull, rpv, i)), p.e_lo));
+        const int ee = int(min(int64_t(__shfl_sync(kFull, rpv, i + 1)), p.e_hi));
+        const float ad_reg = (KH > 0 && lane < KH) ? s.adst[bi][i * KA + lane] : 0.f;
+        float acc[1][8], s_acc[1], inv[1];
+        s_acc[0] = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[0][e] = 0.f;
+        float m_reg = -INFINITY;
+        if (ee > eb)
+          S::row(p, s, c, eb, ee, ad_reg, acc[0], s_acc[0], m_reg, s_col, s_p, hv, lane);
+        inv[0] = (softmax && ee > eb) ? 1.f / (s_acc[0] + p.eps) : 1.f;
+        if (p.fast_epilogue) {
+          A::store_row(p, r, acc, inv, lane);
+        } else {
+          A::spill(p, acc, inv, s_row, lane);
+          __syncwarp();
+          warp_epilogue(p, r, s_row, lane);
+          __syncwarp();
+        }
+      }
+    }
+    // Nothing may still be landing in this warp's buffers when they are reused.
+    cp_async_wait_all();
+    __syncwarp();
+  }
+}
+
 // Edge loop specialised for narrow bf16 rows (32 < F <= 64: one 16-byte load
 // per lane, four edges side by side in 8-lane groups) and a compile-time head
 // count KH (0: GCN edge weights). The scores are formed as in AggFast; each
@@ -969,10 +1286,20 @@ struct EdgeLoop<__nv_bfloat16, 8, 8, 1, -1> {
   using type = Agg<__nv_bfloat16, 8, 8, 1>;
 };
 
-template <typename TH, int VEC, int LPG, int NV, int KH = -1>
+// Floats of the shared-memory carve-up below, before the stream buffers.
+__host__ __device__ constexpr int agg_smem_floats(int F_pad, int HS) {
+  return kWarps * 32 + kWarps * 32 * HS + kWarps * F_pad + 2 * kWarps * kHMax + F_pad +
+         2 * kHMax;
+}
+
+// STREAM: the 256-wide bf16 layout with the prefetched edge stream (AggStream)
+// in both phases; KH >= 0 and GAT or GCN mode only.
+template <typename TH, int VEC, int LPG, int NV, int KH = -1, bool STREAM = false>
 __global__ void __launch_bounds__(kThreads, 4) agg_kernel(const AggParams p) {
   using A = Agg<TH, VEC, LPG, NV>;
   using L = typename EdgeLoop<TH, VEC, LPG, NV, KH>::type;
+  static_assert(!STREAM || (KH >= 0 && LPG == 32 && NV == 1 && VEC == 8), "stream layout");
+  using Win = typename AggStream<(KH >= 0 ? KH : 0)>::Win;
   extern __shared__ float smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -985,6 +1312,9 @@ __global__ void __launch_bounds__(kThreads, 4) agg_kernel(const AggParams p) {
   float* s_fin = s_ws + kWarps * kHMax;                               // F_pad
   float* s_hm = s_fin + p.F_pad;                                      // kHMax
   float* s_hs = s_hm + kHMax;                                         // kHMax
+  // stream buffers, one per warp, 16-byte aligned
+  Win* s_win = reinterpret_cast<Win*>(
+      reinterpret_cast<char*>(smem) + ((agg_smem_floats(p.F_pad, p.HS) * 4 + 15) & ~15));
   __shared__ int s_item;
 
   int32_t* s_col = s_col_all + warp * 32;
@@ -1026,7 +1356,21 @@ __global__ void __launch_bounds__(kThreads, 4) agg_kernel(const AggParams p) {
       for (int e = 0; e < VEC; ++e) acc[v][e] = 0.f;
     }
     float m_reg = -INFINITY;
-    L::range(p, row, wb, we, acc, s_acc, m_reg, s_col, s_p, hv, lane);
+    if constexpr (STREAM) {
+      if (wb < we) {
+        using S = AggStream<(KH >= 0 ? KH : 0)>;
+        const float ad_reg =
+            (KH > 0 && lane < KH) ? __ldg(p.adst + size_t(row) * (KH > 0 ? KH : 1) + lane) : 0.f;
+        typename S::Cursor c;
+        S::begin(p, s_win[warp], c, wb, we, lane);
+        S::row(p, s_win[warp], c, wb, we, ad_reg, acc[0], s_acc[0], m_reg, s_col, s_p, hv[0],
+               lane);
+        cp_async_wait_all();  // nothing left landing in the buffers
+        __syncwarp();
+      }
+    } else {
+      L::range(p, row, wb, we, acc, s_acc, m_reg, s_col, s_p, hv, lane);
+    }
     A::group_reduce(acc, s_acc);
     A::spill(p, acc, one, s_row, lane);
     if (lane < kHMax) s_wm[warp * kHMax + lane] = m_reg;
@@ -1071,6 +1415,9 @@ __global__ void __launch_bounds__(kThreads, 4) agg_kernel(const AggParams p) {
   }
 
   // ---- Phase 2: one warp per short row, edge-balanced row ranges ----
+  if constexpr (STREAM) {
+    stream_tasks<(KH >= 0 ? KH : 0)>(p, s_win[warp], s_col, s_p, s_row, hv[0], lane);
+  } else {
   // (one head or GCN weights: measured faster than the one-row loop; with
   // four heads the per-head group reductions cost more than the overlap gains)
   if constexpr (KH >= 0 && KH <= 1 && LPG == 8 && NV == 1 && VEC == 8) {
@@ -1121,6 +1468,7 @@ __global__ void __launch_bounds__(kThreads, 4) agg_kernel(const AggParams p) {
     }
     }
   }
+  }  // !STREAM
 }
 
 
@@ -1206,9 +1554,19 @@ bool fast_epilogue_ok(const AggParams& p, int vec) {
 // keeps the per-lane stores and the per-head loads free of bank conflicts.
 int head_stride(int mode, int H) { return mode == MODE_GCN ? 1 : (H | 1); }
 
-size_t agg_smem_bytes(int F_pad, int HS) {
-  return sizeof(float) * (size_t(kWarps) * 32 + size_t(kWarps) * 32 * HS +
-                          size_t(kWarps) * F_pad + 2 * kWarps * kHMax + F_pad + 2 * kHMax);
+// stream_kh: the head count of a stream kernel (its per-warp buffers), -1 for none.
+size_t agg_smem_bytes(int F_pad, int HS, int stream_kh = -1) {
+  size_t b = sizeof(float) * size_t(agg_smem_floats(F_pad, HS));
+  if (stream_kh < 0) return b;
+  size_t win = 0;
+  switch (stream_kh) {
+    case 0: win = sizeof(AggStream<0>::Win); break;
+    case 1: win = sizeof(AggStream<1>::Win); break;
+    case 2: win = sizeof(AggStream<2>::Win); break;
+    case 4: win = sizeof(AggStream<4>::Win); break;
+    default: win = sizeof(AggStream<8>::Win); break;
+  }
+  return gnnc::align_up(b, 16) + size_t(kWarps) * win;
 }
 
 int part_stride_floats(int F) { return int(gnnc::align_up(size_t(2 * kHMax + F), 4)); }
@@ -1240,8 +1598,10 @@ struct Launch {
 // The aggregation kernel for a layout: the specialised edge loops where they
 // apply (compile-time head counts for 256-wide bf16 / fp32 rows and narrow
 // bf16 rows), the generic template otherwise; nullptr if there is none.
-KernelFn choose_kernel(const AggParams& p, int h_dtype, int vec, int lpg, int nv) {
+KernelFn choose_kernel(const AggParams& p, int h_dtype, int vec, int lpg, int nv,
+                       int* stream_kh = nullptr) {
   KernelFn fn = nullptr;
+  if (stream_kh) *stream_kh = -1;
   if (h_dtype == GNNC_BF16 && vec == 8 && lpg == 8 && nv == 1) {
     // Narrow rows (32 < F <= 64): specialised loop for a compile-time head count.
     switch (p.mode == MODE_GCN ? 0 : p.H) {
@@ -1263,6 +1623,23 @@ KernelFn choose_kernel(const AggParams& p, int h_dtype, int vec, int lpg, int nv
       case 8: fn = agg_kernel<float, 4, 32, 2, 8>; break;
       default: break;
     }
+  }
+  if (!fn && h_dtype == GNNC_BF16 && vec == 8 && p.F == 256 && p.mode != MODE_SCORES) {
+    // The prefetched edge stream: a_src / a_dst rows are copied whole
+    // (4, 8 or 16-byte cp.async), so both tables must be aligned to that.
+    const int kh = p.mode == MODE_GCN ? 0 : p.H;
+    const size_t row_align = kh == 1 ? 4 : (kh == 2 ? 8 : 16);
+    const bool ok = kh == 0 || (reinterpret_cast<uintptr_t>(p.asrc) % row_align == 0 &&
+                                reinterpret_cast<uintptr_t>(p.adst) % row_align == 0);
+    switch (ok ? kh : -1) {
+      case 0: fn = agg_kernel<__nv_bfloat16, 8, 32, 1, 0, true>; break;
+      case 1: fn = agg_kernel<__nv_bfloat16, 8, 32, 1, 1, true>; break;
+      case 2: fn = agg_kernel<__nv_bfloat16, 8, 32, 1, 2, true>; break;
+      case 4: fn = agg_kernel<__nv_bfloat16, 8, 32, 1, 4, true>; break;
+      case 8: fn = agg_kernel<__nv_bfloat16, 8, 32, 1, 8, true>; break;
+      default: break;
+    }
+    if (fn && stream_kh) *stream_kh = kh;
   }
   if (!fn && h_dtype == GNNC_BF16 && vec == 8 && p.F == 256) {
     // Specialised edge loop for a compile-time head count. It reads a_src
@@ -1299,7 +1676,8 @@ int run_aggregate(gnnc_ctx_t* ctx, const Launch& L, AggParams p) {
     return gnnc::set_error(ctx, GNNC_ERR_UNSUPPORTED,
                            "feature width %d too large for the row kernel (vector width %d)", p.F,
                            vec);
-  KernelFn fn = choose_kernel(p, L.h_dtype, vec, lpg, nv);
+  int stream_kh = -1;
+  KernelFn fn = choose_kernel(p, L.h_dtype, vec, lpg, nv, &stream_kh);
   if (!fn) return gnnc::set_error(ctx, GNNC_ERR_UNSUPPORTED, "no kernel for layout");
 
   p.F_pad = int(gnnc::align_up(size_t(lpg * vec * nv), 4));
@@ -1312,6 +1690,8 @@ int run_aggregate(gnnc_ctx_t* ctx, const Launch& L, AggParams p) {
   p.split_rows = plan->split_rows;
   p.warp_tasks = plan->warp_tasks;
   p.n_warp_tasks = plan->n_warp_tasks;
+  p.stream_tasks = plan->stream_tasks;
+  p.n_stream_tasks = plan->n_stream_tasks;
   p.cta_threshold = wide ? plan->wide_threshold : plan->cta_threshold;
   p.counters = ctx->dev_words;
   p.partials = nullptr;
@@ -1321,7 +1701,7 @@ int run_aggregate(gnnc_ctx_t* ctx, const Launch& L, AggParams p) {
     if (st) return st;
     p.partials = reinterpret_cast<float*>(ctx->ws);
   }
-  const size_t smem = agg_smem_bytes(p.F_pad, p.HS);
+  const size_t smem = agg_smem_bytes(p.F_pad, p.HS, stream_kh);
   if (smem > 48 * 1024)
     GNNC_CUDA_TRY(ctx, cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             int(smem)));
@@ -1450,6 +1830,31 @@ extern "C" int gnnc_plan_create(gnnc_ctx_t* ctx, const int32_t* rowptr, int64_t 
     }
   }
   if (tasks.back() != n_rows) tasks.push_back(int32_t(n_rows));
+  // Stream tasks (wide launches with the prefetched edge stream): runs of
+  // consecutive rows that the wide launches give to warps, cut at every row
+  // they leave to the CTA path, so each task's edges are contiguous.
+  std::vector<int2> stasks;
+  {
+    int64_t c = 0;
+    int64_t start = -1;
+    for (int64_t r = 0; r < n_rows; ++r) {
+      const int deg = rp[r + 1] - rp[r];
+      if (deg > wide_threshold) {
+        if (start >= 0) stasks.push_back(make_int2(int(start), int(r)));
+        start = -1;
+        c = 0;
+        continue;
+      }
+      if (start < 0) start = r;
+      c += deg + kRowCost;
+      if (c >= kTaskCost) {
+        stasks.push_back(make_int2(int(start), int(r + 1)));
+        start = -1;
+        c = 0;
+      }
+    }
+    if (start >= 0) stasks.push_back(make_int2(int(start), int(n_rows)));
+  }
   // Largest CTA items first, so the long ones do not form the tail; whole
   // rows the wide launches leave to warps go last.
   auto warp_on_wide = [&](const int4& it) { return it.w < 0 && it.z - it.y <= wide_threshold; };
@@ -1473,6 +1878,7 @@ extern "C" int gnnc_plan_create(gnnc_ctx_t* ctx, const int32_t* rowptr, int64_t 
   plan->wide_threshold = wide_threshold;
   plan->n_cta_items_wide = n_items_wide;
   plan->n_warp_tasks = int64_t(tasks.size()) - 1;
+  plan->n_stream_tasks = int64_t(stasks.size());
   plan->max_degree = max_deg;
   plan->device = ctx->device;
   plan->e_begin = rp[0];
@@ -1492,6 +1898,9 @@ extern "C" int gnnc_plan_create(gnnc_ctx_t* ctx, const int32_t* rowptr, int64_t 
   if (e == cudaSuccess)
     e = upload(reinterpret_cast<void**>(&plan->warp_tasks), tasks.data(),
                tasks.size() * sizeof(int32_t));
+  if (e == cudaSuccess)
+    e = upload(reinterpret_cast<void**>(&plan->stream_tasks),
+               stasks.empty() ? nullptr : stasks.data(), stasks.size() * sizeof(int2));
   if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
   if (e != cudaSuccess) {
     gnnc_plan_destroy(plan);
@@ -1507,6 +1916,7 @@ extern "C" int gnnc_plan_destroy(gnnc_plan_t* plan) {
   if (plan->cta_items) cudaFree(plan->cta_items);
   if (plan->split_rows) cudaFree(plan->split_rows);
   if (plan->warp_tasks) cudaFree(plan->warp_tasks);
+  if (plan->stream_tasks) cudaFree(plan->stream_tasks);
   delete plan;
   return GNNC_OK;
 }
@@ -1718,7 +2128,8 @@ extern "C" int gnnc_gat_aggregate_noalloc(gnnc_ctx_t* ctx, const gnnc_plan_t* pl
     return gnnc::set_error(ctx, GNNC_ERR_UNSUPPORTED,
                            "feature width %d too large for the row kernel (vector width %d)", p.F,
                            vec);
-  KernelFn fn = choose_kernel(p, h_dtype, vec, lpg, nv);
+  int stream_kh = -1;
+  KernelFn fn = choose_kernel(p, h_dtype, vec, lpg, nv, &stream_kh);
   if (!fn) return gnnc::set_error(ctx, GNNC_ERR_UNSUPPORTED, "no kernel for layout");
   p.F_pad = int(gnnc::align_up(size_t(lpg * vec * nv), 4));
   p.HS = head_stride(p.mode, p.H);
@@ -1730,6 +2141,8 @@ extern "C" int gnnc_gat_aggregate_noalloc(gnnc_ctx_t* ctx, const gnnc_plan_t* pl
   p.split_rows = plan->split_rows;
   p.warp_tasks = plan->warp_tasks;
   p.n_warp_tasks = plan->n_warp_tasks;
+  p.stream_tasks = plan->stream_tasks;
+  p.n_stream_tasks = plan->n_stream_tasks;
   p.cta_threshold = wide ? plan->wide_threshold : plan->cta_threshold;
 
   const size_t need = size_t(plan->n_segments) * p.part_stride * sizeof(float);
@@ -1743,7 +2156,7 @@ extern "C" int gnnc_gat_aggregate_noalloc(gnnc_ctx_t* ctx, const gnnc_plan_t* pl
   p.counters = reinterpret_cast<int*>(scratch);
   p.partials = reinterpret_cast<float*>(scratch + kStaticCounterBytes);
 
-  const size_t smem = agg_smem_bytes(p.F_pad, p.HS);
+  const size_t smem = agg_smem_bytes(p.F_pad, p.HS, stream_kh);
   if (smem > 48 * 1024)
     GNNC_CUDA_TRY(ctx, cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             int(smem)));

@@ -56,6 +56,8 @@ struct gnnc_plan {
   int4* cta_items = nullptr;     // (row, edge_begin, edge_end, slot or -1), largest first
   int4* split_rows = nullptr;    // (row, first_slot, n_slots, 0)
   int32_t* warp_tasks = nullptr; // n_warp_tasks+1 row boundaries
+  int64_t n_stream_tasks = 0;
+  int2* stream_tasks = nullptr;  // row ranges [x, y) of wide-launch warp rows only
 };
 
 namespace gnnc {

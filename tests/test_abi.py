@@ -60,6 +60,9 @@ def test_null_arguments_are_rejected_without_a_device():
     assert lib.gnnc_comm_init(None, None, 0, 1) == _lib.ERR_INVALID
     assert lib.gnnc_allgather(None, None, None, 0, 0) == _lib.ERR_INVALID
     assert lib.gnnc_comm_destroy(None) == _lib.ERR_INVALID
+    assert lib.gnnc_comm_init_timeout(None, None, 0, 1, 1000) == _lib.ERR_INVALID
+    assert lib.gnnc_comm_wait(None, 1000) == _lib.ERR_INVALID
+    assert lib.gnnc_wait_selftest(None, 1000) == _lib.ERR_INVALID
     assert lib.gnnc_plan_destroy(None) == _lib.OK
 
 
