@@ -118,23 +118,16 @@ struct VecLoad<__nv_bfloat16, 1> {
   }
 };
 
-// expm1(v) for v <= 0 (ELU's negative branch, which torch computes as expm1).
-// exp(v) - 1 alone cancels for small |v|, so above -0.5 the Taylor series
-// sum_{k=1..7} v^k / k! is used (truncation error below v^7 / 7! relative,
-// < 2e-7 on (-0.5, 0]), evaluated by Horner's rule; below -0.5, exp(v) <= 0.61
-// and exp(v) - 1 keeps full relative accuracy.
+// expm1(v) for v <= 0 (ELU's negative branch, which torch computes as expm1),
+// without branches. exp(v) - 1 cancels for small |v|: on (-1/64, 0] the Taylor
+// polynomial v + v^2/2 + v^3/6 is used instead (truncation below v^4/24, a
+// relative 1e-7 of the result there). Below -1/64 exp(v) - 1 is used, whose
+// absolute error (that of the fast exponential near 1, a few 1e-7) is a
+// relative error of at most ~2e-5 of |expm1(v)| >= 0.0155, falling with |v|.
 __device__ __forceinline__ float expm1_nonpos(float v) {
-  if (v > -0.5f) {
-    float p = 1.f / 5040.f;
-    p = fmaf(p, v, 1.f / 720.f);
-    p = fmaf(p, v, 1.f / 120.f);
-    p = fmaf(p, v, 1.f / 24.f);
-    p = fmaf(p, v, 1.f / 6.f);
-    p = fmaf(p, v, 0.5f);
-    p = fmaf(p, v, 1.f);
-    return v * p;
-  }
-  return __expf(v) - 1.f;
+  const float taylor = fmaf(v * v, fmaf(v, 1.f / 6.f, 0.5f), v);
+  const float direct = __expf(v) - 1.f;
+  return v > -0.015625f ? taylor : direct;
 }
 
 __device__ __forceinline__ float apply_act(float v, int act) {
@@ -622,7 +615,12 @@ __device__ __forceinline__ void cp_async_wait_all() {
 template <int KH>
 struct AggStream {
   static constexpr int KA = KH == 0 ? 1 : KH;  // floats staged per edge (a_src row or weight)
-  static constexpr int HS = KH == 0 ? 1 : (KH | 1);
+  // The chunk's softmax weights sit head by head in s_p (s_p[hd * PS + edge]),
+  // so that a lane reads four consecutive edges' weights of its head with one
+  // 16-byte load; PS = 36 puts the heads' rows 4 banks apart (conflict-free
+  // for the lanes of different heads). The buffer holds 32 * (KH | 1) floats.
+  static constexpr int PS = KH <= 1 ? 32 : 36;
+  static_assert(KH * PS <= 32 * (KH | 1), "s_p capacity");
 
   // Per-warp shared memory. Window slots are rings indexed by window & 3.
   struct Win {
@@ -710,7 +708,7 @@ struct AggStream {
                                              int lane) {
     const char* hlane = reinterpret_cast<const char*>(p.h) + lane * 16;
     const uint32_t ldh_b = uint32_t(p.ldh) * 2u;
-    const float* s_ph = s_p + hv;
+    const float* s_ph = s_p + hv * PS;
     float sc_reg = 1.f;
     for (int cb = eb; cb < ee; cb += 32) {
       if (cb >= c.base + 32) advance_to(p, s, c, c.w + 1, lane);
@@ -760,7 +758,7 @@ struct AggStream {
             m_reg = m_new;
           }
           rescale |= (cb != eb) && (m_new != m_old);
-          s_p[lane * HS + hd] = pr;
+          s_p[hd * PS + lane] = pr;
         }
         if (rescale) {  // warp-uniform
           const float sc = __shfl_sync(kFull, sc_reg, hv);
@@ -773,25 +771,43 @@ struct AggStream {
       const int n = min(32, ee - cb);
       int j = 0;
       for (; j + 8 <= n; j += 8) {
-        const int32_t* cj = s_col + j;
-        const float* pj = s_ph + j * HS;
+        // s_col and s_p rows are 16-byte aligned and j is a multiple of 8
+        const int4 c0 = *reinterpret_cast<const int4*>(s_col + j);
+        const int4 c1 = *reinterpret_cast<const int4*>(s_col + j + 4);
+        const int cj[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
         uint4 v[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u)
           v[u] = __ldg(reinterpret_cast<const uint4*>(hlane + size_t(uint32_t(cj[u])) * ldh_b));
+        const float4 q0 = *reinterpret_cast<const float4*>(s_ph + j);
+        const float4 q1 = *reinterpret_cast<const float4*>(s_ph + j + 4);
+        const float pj[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-          const float a = pj[u * HS];
-          s_acc += a;
-          AggFast<KH>::fma_row(acc, a, v[u]);
+          s_acc += pj[u];
+          AggFast<KH>::fma_row(acc, pj[u], v[u]);
         }
       }
-      for (; j < n; ++j) {
-        const uint4 v =
-            __ldg(reinterpret_cast<const uint4*>(hlane + size_t(uint32_t(s_col[j])) * ldh_b));
-        const float a = s_ph[j * HS];
-        s_acc += a;
-        AggFast<KH>::fma_row(acc, a, v);
+      if (j < n) {
+        // The last 1-7 edges: their row loads go out together (one round
+        // trip, not one per edge), then fold in edge order.
+        const int rem = n - j;
+        uint4 v[7];
+#pragma unroll
+        for (int u = 0; u < 7; ++u) {
+          v[u] = make_uint4(0u, 0u, 0u, 0u);
+          if (u < rem)
+            v[u] = __ldg(
+                reinterpret_cast<const uint4*>(hlane + size_t(uint32_t(s_col[j + u])) * ldh_b));
+        }
+#pragma unroll
+        for (int u = 0; u < 7; ++u) {
+          if (u < rem) {
+            const float a = s_ph[j + u];
+            s_acc += a;
+            AggFast<KH>::fma_row(acc, a, v[u]);
+          }
+        }
       }
       __syncwarp();
     }
