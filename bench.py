@@ -126,30 +126,38 @@ def ncu_traffic(workload: str) -> dict:
     return out
 
 
-def roofline(kernel: str, workload: str, bytes_alg: float, agg_ms: float, world: int) -> dict:
+def roofline(kernel: str, workload: str, bytes_alg: float, agg_ms: float, world: int,
+             edge_share: float = 1.0) -> dict:
     """Roofline of the aggregation kernel. Primary figure: measured DRAM bytes
     per launch (ncu, this kernel source, one GPU) over the CUDA-event duration;
-    beside it the edge-gather model, an upper count that includes L2 hits."""
+    beside it the edge-gather model, an upper count that includes L2 hits.
+
+    At N > 1 a rank's launch covers `edge_share` of the edges: its DRAM bytes
+    are the one-GPU capture scaled by that share. A rank's rows draw on the
+    whole h table with the same hot sources, each hot row read 1/N as often
+    in 1/N of the time, so the L2 hit rate and the bytes per edge stay those
+    of the one-GPU launch."""
     peak, peak_kind = hbm_peak()
     t = agg_ms / 1e3
     alg = bytes_alg / t / 1e9
     tr = ncu_traffic(workload)
-    use_dram = tr["current"] and world == 1
+    use_dram = tr["current"]
     line = {
         "bound": "hbm",
         "kernel": kernel,
-        "basis": "dram" if use_dram else "edge-gather (upper count: includes L2 hits)",
+        "basis": (("dram" if world == 1 else "dram (one-GPU capture x this rank's edge share)")
+                  if use_dram else "edge-gather (upper count: includes L2 hits)"),
         "achieved": None,
         "peak": peak,
         "peak_source": (f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
                         else "fallback 6.65 TB/s"),
         "unit": "GB/s",
         "frac": None,
-        "traffic": tr["bytes"] if use_dram else None,
+        "traffic": round(tr["bytes"] * edge_share) if use_dram else None,
         "traffic_source": {**tr, "note": (
             "ncu dram__bytes_read.sum + dram__bytes_write.sum, one full-size launch on one GPU"
-            if world == 1 else
-            "not used: the capture is of the one-GPU launch, not of this rank's share")},
+            + ("" if world == 1 else
+               f"; scaled by this rank's share of the edges ({edge_share:.4f})"))},
         "launch_ms": agg_ms,
         "algorithmic": {
             "bytes_per_launch": bytes_alg,
@@ -161,7 +169,7 @@ def roofline(kernel: str, workload: str, bytes_alg: float, agg_ms: float, world:
         },
     }
     if use_dram:
-        dram = tr["bytes"] / t / 1e9
+        dram = tr["bytes"] * edge_share / t / 1e9
         line.update(achieved=dram, frac=dram / peak, achieved_dram=dram, frac_dram=dram / peak)
     else:
         line.update(achieved=alg, frac=alg / peak, achieved_dram=None, frac_dram=None)
@@ -561,7 +569,7 @@ def run_b200(args) -> None:
             "layer_ms": {"projection": float(g[worst, 2]), "aggregation": agg_worst,
                          "step": total_max / K},
             "roofline": roofline("gnnc_gat_aggregate (agg_kernel + merge_kernel)", WORKLOAD,
-                                 bytes_worst, agg_worst, world),
+                                 bytes_worst, agg_worst, world, float(g[worst, 4]) / E),
             "gpu_launches": launches_per_step * K,
             "clocks": clocks,
             "e2e": e2e,
@@ -705,7 +713,7 @@ def run_c5(args) -> None:
                 "check": check,
             },
             "roofline": roofline("gnnc_gat_aggregate (agg_kernel + merge_kernel)", C5,
-                                 float(gs[worst, 1]), ms_max / K, world),
+                                 float(gs[worst, 1]), ms_max / K, world, float(gs[worst, 2]) / E),
             "gpu_launches": (1 + (1 if info["n_split_rows"] > 0 else 0)) * K,
             "clocks": clocks,
             "e2e": None,

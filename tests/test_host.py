@@ -193,8 +193,9 @@ def test_bench_roofline_uses_dram_bytes_of_the_current_kernel_only(tmp_path, mon
     assert r["basis"] == "dram" and r["traffic"] == 20_000_000_000
     assert abs(r["achieved"] - 20.0e9 / 4e-3 / 1e9) < 1e-6 and r["frac"] == r["frac_dram"]
     assert r["algorithmic"]["achieved"] > r["achieved"]
-    r2 = bench.roofline("k", bench.WORKLOAD, 35.0e9, 4.0, 2)  # a rank's share: not that capture
-    assert r2["traffic"] is None and r2["frac_dram"] is None and r2["basis"].startswith("edge-gather")
+    r2 = bench.roofline("k", bench.WORKLOAD, 17.5e9, 2.0, 2, 0.5)  # a rank's half of the edges
+    assert r2["traffic"] == 10_000_000_000 and r2["basis"].startswith("dram (one-GPU capture")
+    assert abs(r2["achieved"] - 10.0e9 / 2e-3 / 1e9) < 1e-6
     prof.write_text("dram_bytes_per_launch_full_size: 20.0e9 bytes\nkernel_source_sha256_16: 0000\n")
     r3 = bench.roofline("k", bench.WORKLOAD, 35.0e9, 4.0, 1)  # stale capture
     assert r3["traffic"] is None and not r3["traffic_source"]["current"]
