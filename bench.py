@@ -17,7 +17,9 @@ cross NVLink (208 bytes a row instead of the 528 of h and a_src): the copy
 engines pull the other ranks' rows from their HBM (CUDA IPC mappings) in
 pieces on a side stream while the projection of the pieces already present
 runs, every rank projects all rows, and each rank aggregates its own rows with
-the single-GPU plan's split decisions.
+the single-GPU plan's split decisions. Two one-word NCCL all-reduces per step
+order the owners' writes of their input rows before the pulls, and the pulls
+before the next step's writes (the second one after the aggregation).
 
 Printed (rank 0, one JSON line): value = stored edges x steps / device time
 (max over ranks); e2e = the same metric through gnnc.execution.run_jit with
@@ -338,6 +340,9 @@ class OneGpu:
                      out_dtype=torch.bfloat16, out=self.h_full, asrc_out=self.a_full,
                      adst_out=self.adst_l)
 
+    def finish(self):
+        pass
+
     def close(self):
         pass
 
@@ -349,7 +354,8 @@ class PeerExchange:
     remote rows over NVLink (no SM used) into a local table, piece by piece on
     a side stream, while the projection runs on the rows already present (its
     own rows first); then the rank aggregates its own rows. Two one-word NCCL
-    all-reduces per step order the input writes and the peers' reads."""
+    all-reduces per step order the input writes and the peers' reads: one at
+    the start of project(), one in finish() after the aggregation."""
 
     PIECE_ROWS = 1 << 18
 
@@ -413,7 +419,13 @@ class PeerExchange:
         for (p, a, b), ev in zip(self.pieces, self.piece_ev):
             cur.wait_event(ev)
             self._proj(self.stage[p * R + a : p * R + b, :IN], slice(p * R + a, p * R + b))
-        self.fence()  # every rank is done reading (the owners may overwrite)
+
+    def finish(self):
+        """After the step's aggregation: every rank is done reading the owners'
+        input rows (its pulls completed before its last projection), so the
+        owners may overwrite them. Placed after the aggregation, the wait for
+        the slowest reader does not delay this rank's aggregation."""
+        self.fence()
 
     def close(self):
         self.peers.close()
@@ -472,9 +484,13 @@ def run_b200(args) -> None:
                          heads=HEADS, concat=True, bias=bias, act=rt.ACT_ELU,
                          out_dtype=torch.bfloat16, out=out_l)
 
-    for _ in range(args.warmup):
+    def step():
         project()
         aggregate()
+        lay.finish()
+
+    for _ in range(args.warmup):
+        step()
     rt.Context.get(device).synchronize()
 
     K = args.steps
@@ -494,6 +510,7 @@ def run_b200(args) -> None:
         ev[i][1].record()
         aggregate()
         ev[i][2].record()
+        lay.finish()
     t_end.record()
     torch.cuda.synchronize(device)
     if world > 1:
@@ -783,6 +800,7 @@ def e2e_b200(args, layer, ei_host, x_host, device, world, N, E, project, aggrega
             x_dev.copy_(x_pin, non_blocking=True)
             project()
             aggregate()
+            lay.finish()
             out_pin.copy_(out_l, non_blocking=True)
         e.record()
         torch.cuda.synchronize(device)

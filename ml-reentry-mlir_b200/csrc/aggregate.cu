@@ -1815,8 +1815,14 @@ extern "C" int gnnc_plan_create(gnnc_ctx_t* ctx, const int32_t* rowptr, int64_t 
   int64_t n_warp = 0, n_cta = 0, n_seg = 0;
   int max_deg = 0;
   // Warp tasks: contiguous row ranges of roughly equal cost (edges + a fixed
-  // per-row overhead); rows taken by the CTA path cost one unit.
-  const int64_t kTaskCost = 768, kRowCost = 6;
+  // per-row overhead); rows taken by the CTA path cost one unit. A task costs
+  // 768 units, or less on small launches (a rank's share of a partitioned
+  // graph) so that every resident warp gets about eight tasks and the last
+  // ones finish together.
+  const int64_t kRowCost = 6;
+  const int64_t total_cost = (int64_t(rp[size_t(n_rows)]) - rp[0]) + kRowCost * n_rows;
+  const int64_t kTaskCost = std::min<int64_t>(
+      768, std::max<int64_t>(192, total_cost / (int64_t(ctx->num_sms) * 32 * 8)));
   int64_t cost = 0;
   tasks.push_back(0);
   for (int64_t r = 0; r < n_rows; ++r) {
