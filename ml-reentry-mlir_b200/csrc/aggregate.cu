@@ -1302,6 +1302,66 @@ struct EdgeLoop<__nv_bfloat16, 8, 8, 1, -1> {
   using type = Agg<__nv_bfloat16, 8, 8, 1>;
 };
 
+// Phase 2 of agg_kernel without the edge stream: warps pull edge-balanced row
+// ranges and process their rows one at a time with the layout's edge loop.
+template <typename TH, int VEC, int LPG, int NV, int KH>
+__device__ __forceinline__ void warp_rows(const AggParams& p, int32_t* s_col, float* s_p,
+                                          float* s_row, const int (&hv)[NV], int lane) {
+  using A = Agg<TH, VEC, LPG, NV>;
+  using L = typename EdgeLoop<TH, VEC, LPG, NV, KH>::type;
+  const bool softmax = p.mode != MODE_GCN;
+  // (one head or GCN weights: measured faster than the one-row loop; with
+  // four heads the per-head group reductions cost more than the overlap gains)
+  if constexpr (KH >= 0 && KH <= 1 && LPG == 8 && NV == 1 && VEC == 8) {
+    if (p.concat || p.H == 1) {
+      narrow_rows<KH>(p, s_col, s_p, lane, softmax);
+      return;
+    }
+  }
+  for (;;) {
+    int t = 0;
+    if (lane == 0) t = atomicAdd(p.counters + 1, 1);
+    t = __shfl_sync(kFull, t, 0);
+    if (t >= p.n_warp_tasks) break;
+    const int r0 = p.warp_tasks[t], r1 = p.warp_tasks[t + 1];
+    // The task's row pointers come in with one load per 31 rows (lane i holds
+    // rowptr[rb + i]) instead of two dependent loads at the head of each row.
+    for (int rb = r0; rb < r1; rb += 31) {
+      const int nr = min(31, r1 - rb);
+      const int rpv = lane <= nr ? __ldg(p.rowptr + rb + lane) : 0;
+      for (int i = 0; i < nr; ++i) {
+        const int r = rb + i;
+        const int eb = max(int64_t(__shfl_sync(kFull, rpv, i)), p.e_lo);
+        const int ee = min(int64_t(__shfl_sync(kFull, rpv, i + 1)), p.e_hi);
+        if (ee - eb > p.cta_threshold) continue;
+        float acc[NV][VEC], s_acc[NV], inv[NV];
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+          s_acc[v] = 0.f;
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) acc[v][e] = 0.f;
+        }
+        float m_reg = -INFINITY;
+        if (ee > eb) {
+          L::range(p, r, eb, ee, acc, s_acc, m_reg, s_col, s_p, hv, lane);
+          A::group_reduce(acc, s_acc);
+        }
+        const bool divide = softmax && ee > eb;
+#pragma unroll
+        for (int v = 0; v < NV; ++v) inv[v] = divide ? 1.f / (s_acc[v] + p.eps) : 1.f;
+        if (p.fast_epilogue) {
+          A::store_row(p, r, acc, inv, lane);
+        } else {
+          A::spill(p, acc, inv, s_row, lane);
+          __syncwarp();
+          warp_epilogue(p, r, s_row, lane);
+          __syncwarp();
+        }
+      }
+    }
+  }
+}
+
 // Floats of the shared-memory carve-up below, before the stream buffers.
 __host__ __device__ constexpr int agg_smem_floats(int F_pad, int HS) {
   return kWarps * 32 + kWarps * 32 * HS + kWarps * F_pad + 2 * kWarps * kHMax + F_pad +
@@ -1434,57 +1494,8 @@ __global__ void __launch_bounds__(kThreads, 4) agg_kernel(const AggParams p) {
   if constexpr (STREAM) {
     stream_tasks<(KH >= 0 ? KH : 0)>(p, s_win[warp], s_col, s_p, s_row, hv[0], lane);
   } else {
-  // (one head or GCN weights: measured faster than the one-row loop; with
-  // four heads the per-head group reductions cost more than the overlap gains)
-  if constexpr (KH >= 0 && KH <= 1 && LPG == 8 && NV == 1 && VEC == 8) {
-    if (p.concat || p.H == 1) {
-      narrow_rows<KH>(p, s_col, s_p, lane, softmax);
-      return;
-    }
+    warp_rows<TH, VEC, LPG, NV, KH>(p, s_col, s_p, s_row, hv, lane);
   }
-  for (;;) {
-    int t = 0;
-    if (lane == 0) t = atomicAdd(p.counters + 1, 1);
-    t = __shfl_sync(kFull, t, 0);
-    if (t >= p.n_warp_tasks) break;
-    const int r0 = p.warp_tasks[t], r1 = p.warp_tasks[t + 1];
-    // The task's row pointers come in with one load per 31 rows (lane i holds
-    // rowptr[rb + i]) instead of two dependent loads at the head of each row.
-    for (int rb = r0; rb < r1; rb += 31) {
-    const int nr = min(31, r1 - rb);
-    const int rpv = lane <= nr ? __ldg(p.rowptr + rb + lane) : 0;
-    for (int i = 0; i < nr; ++i) {
-      const int r = rb + i;
-      const int eb = max(int64_t(__shfl_sync(kFull, rpv, i)), p.e_lo);
-      const int ee = min(int64_t(__shfl_sync(kFull, rpv, i + 1)), p.e_hi);
-      if (ee - eb > p.cta_threshold) continue;
-      float acc[NV][VEC], s_acc[NV], inv[NV];
-#pragma unroll
-      for (int v = 0; v < NV; ++v) {
-        s_acc[v] = 0.f;
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) acc[v][e] = 0.f;
-      }
-      float m_reg = -INFINITY;
-      if (ee > eb) {
-        L::range(p, r, eb, ee, acc, s_acc, m_reg, s_col, s_p, hv, lane);
-        A::group_reduce(acc, s_acc);
-      }
-      const bool divide = softmax && ee > eb;
-#pragma unroll
-      for (int v = 0; v < NV; ++v) inv[v] = divide ? 1.f / (s_acc[v] + p.eps) : 1.f;
-      if (p.fast_epilogue) {
-        A::store_row(p, r, acc, inv, lane);
-      } else {
-        A::spill(p, acc, inv, s_row, lane);
-        __syncwarp();
-        warp_epilogue(p, r, s_row, lane);
-        __syncwarp();
-      }
-    }
-    }
-  }
-  }  // !STREAM
 }
 
 
