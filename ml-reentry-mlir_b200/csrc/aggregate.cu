@@ -699,6 +699,22 @@ struct AggStream {
     cp_async_commit();
   }
 
+  // R edges (compile-time count): R row loads in flight, then R FMAs in order.
+  template <int R>
+  static __device__ __forceinline__ void tail(const int32_t* cj, const float* pj,
+                                              const char* hlane, uint32_t ldh_b,
+                                              float (&acc)[8], float& s_acc) {
+    uint4 v[R];
+#pragma unroll
+    for (int u = 0; u < R; ++u)
+      v[u] = __ldg(reinterpret_cast<const uint4*>(hlane + size_t(uint32_t(cj[u])) * ldh_b));
+#pragma unroll
+    for (int u = 0; u < R; ++u) {
+      s_acc += pj[u];
+      AggFast<KH>::fma_row(acc, pj[u], v[u]);
+    }
+  }
+
   // Accumulates the row's edges [eb, ee), which must be the next edges of
   // the stream, in 32-edge chunks counted from eb. ad_reg: lane hd holds
   // a_dst of head hd. Same arithmetic and order as AggFast<KH>::range.
@@ -788,26 +804,18 @@ struct AggStream {
           AggFast<KH>::fma_row(acc, pj[u], v[u]);
         }
       }
-      if (j < n) {
-        // The last 1-7 edges: their row loads go out together (one round
-        // trip, not one per edge), then fold in edge order.
-        const int rem = n - j;
-        uint4 v[7];
-#pragma unroll
-        for (int u = 0; u < 7; ++u) {
-          v[u] = make_uint4(0u, 0u, 0u, 0u);
-          if (u < rem)
-            v[u] = __ldg(
-                reinterpret_cast<const uint4*>(hlane + size_t(uint32_t(s_col[j + u])) * ldh_b));
-        }
-#pragma unroll
-        for (int u = 0; u < 7; ++u) {
-          if (u < rem) {
-            const float a = s_ph[j + u];
-            s_acc += a;
-            AggFast<KH>::fma_row(acc, a, v[u]);
-          }
-        }
+      // The last 1-7 edges: their row loads go out together (one round trip,
+      // not one per edge), then fold in edge order. The count is the same in
+      // every lane, so each case issues exactly its loads and FMAs.
+      switch (n - j) {
+        case 1: tail<1>(s_col + j, s_ph + j, hlane, ldh_b, acc, s_acc); break;
+        case 2: tail<2>(s_col + j, s_ph + j, hlane, ldh_b, acc, s_acc); break;
+        case 3: tail<3>(s_col + j, s_ph + j, hlane, ldh_b, acc, s_acc); break;
+        case 4: tail<4>(s_col + j, s_ph + j, hlane, ldh_b, acc, s_acc); break;
+        case 5: tail<5>(s_col + j, s_ph + j, hlane, ldh_b, acc, s_acc); break;
+        case 6: tail<6>(s_col + j, s_ph + j, hlane, ldh_b, acc, s_acc); break;
+        case 7: tail<7>(s_col + j, s_ph + j, hlane, ldh_b, acc, s_acc); break;
+        default: break;
       }
       __syncwarp();
     }
@@ -891,7 +899,8 @@ __device__ __forceinline__ void stream_tasks(const AggParams& p, typename AggStr
         float m_reg = -INFINITY;
         if (ee > eb)
           S::row(p, s, c, eb, ee, ad_reg, acc[0], s_acc[0], m_reg, s_col, s_p, hv, lane);
-        inv[0] = (softmax && ee > eb) ? 1.f / (s_acc[0] + p.eps) : 1.f;
+        // correctly rounded reciprocal: the same value as 1.f / x
+        inv[0] = (softmax && ee > eb) ? __frcp_rn(s_acc[0] + p.eps) : 1.f;
         if (p.fast_epilogue) {
           A::store_row(p, r, acc, inv, lane);
         } else {
