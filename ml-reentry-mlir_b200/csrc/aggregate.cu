@@ -699,6 +699,62 @@ struct AggStream {
     cp_async_commit();
   }
 
+  // Row epilogue for concatenated heads, bf16 output, no root term: the lane's
+  // 8 features are scaled, biased and activated as fp32 pairs (f32x2), with
+  // the same per-element operations and rounding as Agg::store_row.
+  static __device__ __forceinline__ uint64_t pk(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+  }
+  static __device__ __forceinline__ void upk(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  }
+  static __device__ __forceinline__ void store_bf16(const AggParams& p, int64_t row,
+                                                    const float (&acc)[8], float inv, int lane) {
+    const int e0 = lane * 8;
+    uint64_t o[4];
+    const uint64_t ii = pk(inv, inv);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      o[i] = pk(acc[2 * i], acc[2 * i + 1]);
+      asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(o[i]) : "l"(ii));
+    }
+    if (p.bias) {
+      const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.bias + e0));
+      const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.bias + e0 + 4));
+      const uint64_t bb[4] = {pk(b0.x, b0.y), pk(b0.z, b0.w), pk(b1.x, b1.y), pk(b1.z, b1.w)};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) asm("add.rn.f32x2 %0, %0, %1;" : "+l"(o[i]) : "l"(bb[i]));
+    }
+    float v[8];
+    if (p.act == GNNC_ACT_ELU) {
+      const uint64_t c6 = pk(1.f / 6.f, 1.f / 6.f), c5 = pk(0.5f, 0.5f);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        // expm1_nonpos on both halves: v + v^2 (1/2 + v/6) and exp(v) - 1
+        uint64_t vv, t, taylor;
+        asm("mul.rn.f32x2 %0, %1, %1;" : "=l"(vv) : "l"(o[i]));
+        asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(t) : "l"(o[i]), "l"(c6), "l"(c5));
+        asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(taylor) : "l"(vv), "l"(t), "l"(o[i]));
+        float x0, x1, t0, t1;
+        upk(o[i], x0, x1);
+        upk(taylor, t0, t1);
+        const float d0 = __expf(x0) - 1.f, d1 = __expf(x1) - 1.f;
+        v[2 * i] = x0 > 0.f ? x0 : (x0 > -0.015625f ? t0 : d0);
+        v[2 * i + 1] = x1 > 0.f ? x1 : (x1 > -0.015625f ? t1 : d1);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        upk(o[i], v[2 * i], v[2 * i + 1]);
+        v[2 * i] = apply_act(v[2 * i], p.act);
+        v[2 * i + 1] = apply_act(v[2 * i + 1], p.act);
+      }
+    }
+    store_vec<8>(p.out, GNNC_BF16, size_t(row) * size_t(p.ldo) + e0, v);
+  }
+
   // R edges (compile-time count): R row loads in flight, then R FMAs in order.
   template <int R>
   static __device__ __forceinline__ void tail(const int32_t* cj, const float* pj,
@@ -834,6 +890,7 @@ __device__ __forceinline__ void stream_tasks(const AggParams& p, typename AggStr
   using A = Agg<__nv_bfloat16, 8, 32, 1>;
   constexpr int KA = S::KA;
   const bool softmax = p.mode != MODE_GCN;
+  const bool bf16_epilogue = p.fast_epilogue && !p.root && p.out_dtype == GNNC_BF16;
   for (;;) {
     int t = 0;
     if (lane == 0) t = atomicAdd(p.counters + 1, 1);
@@ -901,7 +958,9 @@ __device__ __forceinline__ void stream_tasks(const AggParams& p, typename AggStr
           S::row(p, s, c, eb, ee, ad_reg, acc[0], s_acc[0], m_reg, s_col, s_p, hv, lane);
         // correctly rounded reciprocal: the same value as 1.f / x
         inv[0] = (softmax && ee > eb) ? __frcp_rn(s_acc[0] + p.eps) : 1.f;
-        if (p.fast_epilogue) {
+        if (bf16_epilogue) {
+          S::store_bf16(p, r, acc[0], inv[0], lane);
+        } else if (p.fast_epilogue) {
           A::store_row(p, r, acc, inv, lane);
         } else {
           A::spill(p, acc, inv, s_row, lane);
