@@ -811,26 +811,44 @@ struct AggStream {
           for (int hd = 0; hd < KH; ++hd) x[hd] = xs[hd];
         }
         bool rescale = false;
+        if (cb == eb) {
+          // A row's first chunk: the running max starts at this chunk's max
+          // (the general step below with m_old = -inf, nothing to rescale).
 #pragma unroll
-        for (int hd = 0; hd < KH; ++hd) {
-          // every lane takes part in the shuffles and the reduction
-          const float ad = __shfl_sync(kFull, ad_reg, hd);
-          float e = -INFINITY;
-          if (valid) {
-            const float t = x[hd] + ad;
-            e = t > 0.f ? t : t * p.slope;
+          for (int hd = 0; hd < KH; ++hd) {
+            const float ad = __shfl_sync(kFull, ad_reg, hd);
+            float e = -INFINITY;
+            if (valid) {
+              const float t = x[hd] + ad;
+              e = t > 0.f ? t : t * p.slope;
+            }
+            const float m_new = warp_max_redux(e);
+            const float pr = valid ? __expf(e - m_new) : 0.f;
+            if (lane == hd) m_reg = m_new;
+            s_p[hd * PS + lane] = pr;
           }
-          const float cmax = warp_max_redux(e);
-          const float m_old = __shfl_sync(kFull, m_reg, hd);
-          const float m_new = fmaxf(m_old, cmax);
-          const float pr = valid ? __expf(e - m_new) : 0.f;
-          const float sc = __expf(m_old - m_new);
-          if (lane == hd) {
-            sc_reg = sc;
-            m_reg = m_new;
+        } else {
+#pragma unroll
+          for (int hd = 0; hd < KH; ++hd) {
+            // every lane takes part in the shuffles and the reduction
+            const float ad = __shfl_sync(kFull, ad_reg, hd);
+            float e = -INFINITY;
+            if (valid) {
+              const float t = x[hd] + ad;
+              e = t > 0.f ? t : t * p.slope;
+            }
+            const float cmax = warp_max_redux(e);
+            const float m_old = __shfl_sync(kFull, m_reg, hd);
+            const float m_new = fmaxf(m_old, cmax);
+            const float pr = valid ? __expf(e - m_new) : 0.f;
+            const float sc = __expf(m_old - m_new);
+            if (lane == hd) {
+              sc_reg = sc;
+              m_reg = m_new;
+            }
+            rescale |= m_new != m_old;
+            s_p[hd * PS + lane] = pr;
           }
-          rescale |= (cb != eb) && (m_new != m_old);
-          s_p[hd * PS + lane] = pr;
         }
         if (rescale) {  // warp-uniform
           const float sc = __shfl_sync(kFull, sc_reg, hv);
