@@ -970,7 +970,7 @@ def cpu_leg_c5(rowptr_d, col_d, h, asrc, adst, out_dev, info, args):
     parity = cpu = None
     t0 = time.time()
     if args.check:
-        local, src, _ = PY._row_edges(rowptr, col, rows)
+        local, src, _ = PY.row_edges(rowptr, col, rows)
         uniq, inv = torch.unique(src, return_inverse=True)
         ud = uniq.to(h.device)
         ref = PY.gat_rows_given_fp64(local, inv, h[ud].cpu(), asrc[ud].cpu(),

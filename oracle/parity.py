@@ -60,8 +60,9 @@ def csr_by_destination(edge_index: torch.Tensor, num_nodes: int):
     return rowptr, key % n
 
 
-def _row_edges(rowptr, col, rows):
-    """(local CSR rowptr over `rows`, global source id of every edge)."""
+def row_edges(rowptr, col, rows):
+    """The edges of destination `rows` as a row-local CSR: (local rowptr over
+    `rows`, global source id of every edge, each edge's index in `col`)."""
     rowptr = torch.as_tensor(rowptr, dtype=torch.int64)
     starts, ends = rowptr[rows], rowptr[rows + 1]
     lens = ends - starts
@@ -132,7 +133,7 @@ def gat_conv_rows_fp64(x, rowptr, col, rows, weight, att_src, att_dst, bias, hea
     rows = torch.as_tensor(rows, dtype=torch.int64)
     H = heads
     C = weight.size(0) // H
-    local, src, _ = _row_edges(rowptr, col, rows)
+    local, src, _ = row_edges(rowptr, col, rows)
     uniq, inv = torch.unique(src, return_inverse=True)
     h_u = _project(x[uniq], weight)  # gat.1-raw-torch.mlir:5-10
     a_s = torch.einsum("uhc,hc->uh", h_u.view(-1, H, C), att_src.double().view(H, C))  # :11-17
@@ -147,7 +148,7 @@ def gcn_conv_rows_fp64(x, rowptr, col, w, rows, weight, bias, *, act=None, log_s
     SpMM, + bias, activation) in float64 for destination `rows`
     (test/reference/gcn.raw.mlir:6-10)."""
     rows = torch.as_tensor(rows, dtype=torch.int64)
-    local, src, k = _row_edges(rowptr, col, rows)
+    local, src, k = row_edges(rowptr, col, rows)
     uniq, inv = torch.unique(src, return_inverse=True)
     h_u = _project(x[uniq], weight)
     out = _weighted_rows(local, inv, torch.as_tensor(w)[k], h_u)
