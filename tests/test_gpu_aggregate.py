@@ -398,3 +398,52 @@ def test_partition_plans_split_like_the_whole_graph(device):
         assert plan.info()["n_split_rows"] == int((deg[rr.begin : rr.end] > thr).sum())
         out = rt.gat_aggregate(plan, rp_l, col_l, h, a, d[rr.begin : rr.end], **kw)
         assert torch.equal(out, full[rr.begin : rr.end]), f"rank {r}"
+
+
+@pytest.mark.parametrize("heads", [4, 0])
+def test_edge_stream_with_empty_rows_hubs_and_splits(device, heads):
+    """The prefetched edge stream (256-wide bf16 rows, GAT and GCN modes) over
+    runs of rows without edges (inside tasks, at task starts and ends), hub
+    rows the plan gives to the CTA path (which cut the stream tasks) and rows
+    split across CTAs, against the oracle."""
+    from gnnc.b200 import runtime as rt
+
+    n = 20_000
+    g = torch.Generator().manual_seed(77)
+    # sources 0..n-1, destinations only in the first ~60 % of rows and a few hubs
+    dst = torch.randint(0, int(n * 0.6), (90_000,), generator=g)
+    src = torch.randint(0, n, (90_000,), generator=g)
+    hubs = [(n - 3, 6000), (n // 2, 2500), (100, 1500)]
+    parts = [torch.stack([src, dst])]
+    for node, deg in hubs:
+        parts.append(torch.stack([torch.randint(0, n, (deg,), generator=g),
+                                  torch.full((deg,), node)]))
+    ei = torch.cat(parts, 1)
+    rowptr, col, mult = rt.csr_from_coo(ei.to(device), n, self_loops=False, dedupe=heads == 0)
+    deg = rowptr.diff().cpu()
+    assert int((deg == 0).sum()) > 5000 and int(deg.max()) >= 6000
+    plan = rt.Plan(rowptr, cta_threshold=0, split_threshold=4096)
+    assert plan.info()["n_split_rows"] >= 1
+    F = 256
+    h_host = torch.randn(n, F, generator=g).to(torch.bfloat16)
+    h = rt.empty_rows(n, F, torch.bfloat16, device)
+    h.copy_(h_host)
+    bias = torch.randn(F, generator=g)
+    if heads:
+        asrc = torch.randn(n, heads, generator=g)
+        adst = torch.randn(n, heads, generator=g)
+        out = rt.gat_aggregate(plan, rowptr, col, h, asrc.to(device), adst.to(device), heads=heads,
+                               bias=bias.to(device), act=rt.ACT_ELU, out_dtype=torch.bfloat16)
+        ref = O.gat_rows_fp64(rowptr.cpu(), col.cpu(), h_host.double(), asrc, adst, heads,
+                              bias=bias, act="elu")
+    else:
+        w = torch.rand(col.numel(), generator=g).to(device)
+        out = rt.gcn_aggregate(plan, rowptr, col, w, h, bias=bias.to(device), act=rt.ACT_RELU,
+                               out_dtype=torch.bfloat16)
+        ref = O.gcn_rows_fp64(rowptr.cpu(), col.cpu(), w.cpu(), h_host.double(), bias=bias,
+                              act="relu")
+    assert_close(out, ref, rtol=2e-2, atol=2e-2)
+    empty = deg == 0
+    expect = torch.nn.functional.elu(bias) if heads else torch.relu(bias)
+    assert torch.allclose(out.float().cpu()[empty], expect.expand(int(empty.sum()), F),
+                          rtol=1e-2, atol=1e-2)
