@@ -421,7 +421,7 @@ def test_edge_stream_with_empty_rows_hubs_and_splits(device, heads):
     ei = torch.cat(parts, 1)
     rowptr, col, mult = rt.csr_from_coo(ei.to(device), n, self_loops=False, dedupe=heads == 0)
     deg = rowptr.diff().cpu()
-    assert int((deg == 0).sum()) > 5000 and int(deg.max()) >= 6000
+    assert int((deg == 0).sum()) > 5000 and int(deg.max()) > 4096
     plan = rt.Plan(rowptr, cta_threshold=0, split_threshold=4096)
     assert plan.info()["n_split_rows"] >= 1
     F = 256
