@@ -14,12 +14,13 @@ attention coefficients a_src, a_dst in its epilogue) and the fused aggregation
 --gpus N (one process per GPU under torchrun) each rank owns a contiguous
 range of destination rows and their input features; the 100-wide input rows
 cross NVLink (208 bytes a row instead of the 528 of h and a_src): the copy
-engines pull the other ranks' rows from their HBM (CUDA IPC mappings) in
-pieces on a side stream while the projection of the pieces already present
-runs, every rank projects all rows, and each rank aggregates its own rows with
-the single-GPU plan's split decisions. Two one-word NCCL all-reduces per step
-order the owners' writes of their input rows before the pulls, and the pulls
-before the next step's writes (the second one after the aggregation).
+engines pull the other ranks' rows from their HBM (CUDA IPC mappings) on a
+side stream, every rank projects all rows, and each rank aggregates its own
+rows with the single-GPU plan's split decisions. The steps are pipelined over
+a stream of batches: batch k+1's pull runs while batch k aggregates (two
+input tables), and one one-word NCCL all-reduce per step orders the owners'
+writes of their input rows and the peers' reads. The timed region ends after
+the last pull it issued.
 
 Printed (rank 0, one JSON line): value = stored edges x steps / device time
 (max over ranks); e2e = the same metric through gnnc.execution.run_jit with
@@ -335,12 +336,17 @@ class OneGpu:
     def node_ids(self):
         return torch.arange(self.n_loc)
 
-    def project(self):
+    def project(self, x_next=None):
+        if x_next is not None:
+            self.x.copy_(x_next, non_blocking=True)
         self.rt.proj(self.x, self.W, att_src=self.att_s, att_dst=self.att_d, heads=HEADS,
                      out_dtype=torch.bfloat16, out=self.h_full, asrc_out=self.a_full,
                      adst_out=self.adst_l)
 
     def finish(self):
+        pass
+
+    def drain(self):
         pass
 
     def close(self):
@@ -349,15 +355,18 @@ class OneGpu:
 
 class PeerExchange:
     """The layer on `world` ranks, reading the remote input rows from the
-    owners' HBM: rank r owns rows [r*R, (r+1)*R) and their input rows; every
-    rank maps the others' input blocks (CUDA IPC). The copy engines pull the
-    remote rows over NVLink (no SM used) into a local table, piece by piece on
-    a side stream, while the projection runs on the rows already present (its
-    own rows first); then the rank aggregates its own rows. Two one-word NCCL
-    all-reduces per step order the input writes and the peers' reads: one at
-    the start of project(), one in finish() after the aggregation."""
+    owners' HBM: rank r owns rows [r*R, (r+1)*R) and their input rows.
 
-    PIECE_ROWS = 1 << 18
+    Each rank keeps two input tables [world*R, ld] (batch k uses table k % 2);
+    its own rows sit in its own slot, and every rank maps the others' tables
+    (CUDA IPC). The steps are pipelined over a stream of batches: batch k is
+    projected (all rows, one launch), then the copy engines pull batch k+1's
+    remote rows over NVLink (no SM used) into the other table while batch k
+    aggregates. One one-word NCCL all-reduce per step orders the buffers: a
+    rank enters it after its pulls of batch k completed and after writing its
+    own rows of batch k+1, and issues the pulls of batch k+1 after it, so an
+    owner never rewrites a slot a peer is still reading and a peer never reads
+    a slot before its owner wrote it."""
 
     def __init__(self, P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device):
         N = x_d.size(0)
@@ -367,10 +376,12 @@ class PeerExchange:
         self.n_loc = rr.count
         self.ld = ld = rt.row_stride(IN, torch.bfloat16)
         R = rr.rows_per_rank
-        self.x_own = torch.zeros((R, ld), dtype=torch.bfloat16, device=device)
-        self.x_own[: rr.count, :IN] = x_d[rr.begin : rr.end]
-        self.peers = P.PeerRows(self.x_own, rr, N)
-        self.stage = torch.empty((world * R, ld), dtype=torch.bfloat16, device=device)
+        self.tables = []
+        for _ in range(2):
+            t = torch.zeros((world * R, ld), dtype=torch.bfloat16, device=device)
+            t[rr.begin : rr.end, :IN] = x_d[rr.begin : rr.end]
+            self.tables.append(t)
+        self.peers = [P.PeerBuffers(t) for t in self.tables]
         self.h_full = rt.empty_rows(world * R, F, torch.bfloat16, device)
         self.a_full = torch.empty((world * R, HEADS), dtype=torch.float32, device=device)
         self.d_full = torch.empty((world * R, HEADS), dtype=torch.float32, device=device)
@@ -378,20 +389,25 @@ class PeerExchange:
         self.n_src = N
         self.W, self.att_s, self.att_d = W, att_s, att_d
         self.fence_buf = torch.zeros(1, dtype=torch.int32, device=device)
-        # (owner, first row, last row) pieces of the remote rows, in read order
-        self.pieces = []
+        # (owner, first table row, end row) of the remote rows, in read order
+        self.pulls = []
         for p in P.read_order(rr)[1:]:
             n_p = P.row_range(N, world, p).count
-            for a in range(0, n_p, self.PIECE_ROWS):
-                self.pieces.append((p, a, min(n_p, a + self.PIECE_ROWS)))
+            self.pulls.append((p, p * R, p * R + n_p))
         self.side = torch.cuda.Stream(device)
-        self.piece_ev = [torch.cuda.Event() for _ in self.pieces]
-        self.proj_launches = 1 + len(self.pieces)
+        self.pulled = [torch.cuda.Event() for _ in range(2)]
+        self.batch = 0
+        self.primed = False
+        self.proj_launches = 1
         self.describe = ("copy-engine pull of remote input rows over NVLink (CUDA IPC peer "
-                         "mapping), pipelined with the projection; no data collective")
+                         "mapping), the next batch's pull overlapping this batch's "
+                         "aggregation; no data collective")
 
     def x_local_rows(self):
-        return self.x_own[: self.n_loc, :IN]
+        """This rank's slot for the input rows that the next project() call
+        sends to the peers (batch k+1 once the pipeline runs)."""
+        t = self.tables[(self.batch + 1) % 2] if self.primed else self.tables[0]
+        return t[self.rr.begin : self.rr.end, :IN]
 
     def node_ids(self):
         return torch.arange(self.rr.begin, self.rr.end)
@@ -399,36 +415,50 @@ class PeerExchange:
     def fence(self):
         dist.all_reduce(self.fence_buf)
 
-    def _proj(self, x, rows: slice):
-        self.rt.proj(x, self.W, att_src=self.att_s, att_dst=self.att_d, heads=HEADS,
-                     out_dtype=torch.bfloat16, out=self.h_full[rows], asrc_out=self.a_full[rows],
-                     adst_out=self.d_full[rows])
-
-    def project(self):
-        R, rt = self.rr.rows_per_rank, self.rt
-        self.fence()  # every rank's input rows are written
-        cur = torch.cuda.current_stream()
-        own = self.rr.rank
-        self.side.wait_stream(cur)
+    def _pull(self, b: int):
+        """Issues the copies of every peer's own rows of table b into this
+        rank's table b on the side stream, after the current stream's work."""
+        self.side.wait_stream(torch.cuda.current_stream())
+        rb = self.ld * 2
         with torch.cuda.stream(self.side):
-            for (p, a, b), ev in zip(self.pieces, self.piece_ev):
-                rt.peer_copy(self.stage[p * R + a :], self.peers.view(p, IN)[a:b],
-                             (b - a) * self.ld * 2)
-                ev.record(self.side)
-        self._proj(self.x_own[: self.n_loc, :IN], slice(own * R, own * R + self.n_loc))
-        for (p, a, b), ev in zip(self.pieces, self.piece_ev):
-            cur.wait_event(ev)
-            self._proj(self.stage[p * R + a : p * R + b, :IN], slice(p * R + a, p * R + b))
+            for p, a, e in self.pulls:
+                self.rt.peer_copy(self.tables[b][a:], self.peers[b].rows(p, a, e), (e - a) * rb)
+            self.pulled[b].record(self.side)
+
+    def project(self, x_next=None):
+        """Projects batch k and starts the pull of batch k+1. `x_next`, when
+        given, is this rank's input rows of batch k+1 (e.g. pinned host rows),
+        copied into its slot before the fence."""
+        if not self.primed:
+            self.fence()  # every rank's input rows of batch 0 are written
+            self._pull(0)
+            self.primed = True
+        b = self.batch % 2
+        cur = torch.cuda.current_stream()
+        cur.wait_event(self.pulled[b])  # batch k's remote rows are present
+        if x_next is not None:
+            self.x_local_rows().copy_(x_next, non_blocking=True)
+        self.fence()
+        self.rt.proj(self.tables[b][: self.N, :IN], self.W, att_src=self.att_s,
+                     att_dst=self.att_d, heads=HEADS, out_dtype=torch.bfloat16,
+                     out=self.h_full[: self.N], asrc_out=self.a_full[: self.N],
+                     adst_out=self.d_full[: self.N])
+        # batch k+1's remote rows, pulled while batch k aggregates
+        self._pull(1 - b)
+        self.batch += 1
 
     def finish(self):
-        """After the step's aggregation: every rank is done reading the owners'
-        input rows (its pulls completed before its last projection), so the
-        owners may overwrite them. Placed after the aggregation, the wait for
-        the slowest reader does not delay this rank's aggregation."""
-        self.fence()
+        pass
+
+    def drain(self):
+        """The current stream waits for the pulls still in flight (the next
+        batch's), so that a timed region ends after every copy it issued."""
+        if self.primed:
+            torch.cuda.current_stream().wait_event(self.pulled[self.batch % 2])
 
     def close(self):
-        self.peers.close()
+        for pb in self.peers:
+            pb.close()
 
 
 def run_b200(args) -> None:
@@ -458,8 +488,6 @@ def run_b200(args) -> None:
     att_d = conv.att_dst.detach().reshape(-1).to(device)
     bias = conv.bias.detach().to(device)
     if world > 1:
-        if args.piece_rows:
-            PeerExchange.PIECE_ROWS = args.piece_rows
         lay = PeerExchange(P, rt, rowptr, col, x_d, W, att_s, att_d, rank, world, device)
     else:
         lay = OneGpu(rt, rowptr, col, x_d, W, att_s, att_d, device)
@@ -511,6 +539,7 @@ def run_b200(args) -> None:
         aggregate()
         ev[i][2].record()
         lay.finish()
+    lay.drain()
     t_end.record()
     torch.cuda.synchronize(device)
     if world > 1:
@@ -790,6 +819,8 @@ def e2e_b200(args, layer, ei_host, x_host, device, world, N, E, project, aggrega
         x_dev = lay.x_local_rows()
         x_pin = torch.empty(tuple(x_dev.shape), dtype=torch.bfloat16, pin_memory=True)
         x_pin.copy_(x_dev.cpu())
+        # every step copies one batch's rows in (the next batch's, once the
+        # exchange is pipelined) and the step's output rows out
         out_pin = torch.empty((lay.n_loc, F), dtype=torch.bfloat16, pin_memory=True)
         s = torch.cuda.Event(enable_timing=True)
         e = torch.cuda.Event(enable_timing=True)
@@ -797,11 +828,11 @@ def e2e_b200(args, layer, ei_host, x_host, device, world, N, E, project, aggrega
         torch.cuda.synchronize(device)
         s.record()
         for _ in range(K):
-            x_dev.copy_(x_pin, non_blocking=True)
-            project()
+            project(x_pin)
             aggregate()
             lay.finish()
             out_pin.copy_(out_l, non_blocking=True)
+        lay.drain()
         e.record()
         torch.cuda.synchronize(device)
         ms = s.elapsed_time(e)
@@ -1075,8 +1106,6 @@ def main() -> None:
                     help="the headline layer (default) or the c5 fused-aggregation microbenchmark")
     ap.add_argument("--cta-threshold", type=int, default=0)
     ap.add_argument("--split-threshold", type=int, default=0)
-    ap.add_argument("--piece-rows", type=int, default=0,
-                    help="N>1: rows per copy-engine piece of the input-row pull (default 2^18)")
     ap.add_argument("--e2e-steps", type=int, default=30)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--ref-step-seconds", type=float, default=0.3)

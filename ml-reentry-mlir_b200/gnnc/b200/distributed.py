@@ -16,7 +16,9 @@ the narrower side of its projection:
   for GAT), and the other slots are pulled the same way.
 
 The layer's aggregation then reads local memory only and writes its rows
-straight into the next layer's input slot. A fence orders each exchanged
+straight into the next layer's input slot. For a stream of batches,
+run_stream pipelines the first layer's input exchange across them: batch
+k+1's rows are pulled into a second table while batch k aggregates. A fence orders each exchanged
 buffer's writes before the peers' reads (a one-word NCCL all-reduce on the
 stream, or a host barrier for gloo process groups that names a rank which
 stopped arriving, `host_fence`), and one more at the end of
@@ -128,6 +130,7 @@ class DistributedExecutable:
         self._layers: list[_Layer] = []
         self._out: torch.Tensor | None = None
         self._rr: P.RowRange | None = None
+        self._second: tuple[torch.Tensor, _PeerTable] | None = None  # run_stream's 2nd table
 
     # -- set-up ------------------------------------------------------------
 
@@ -209,6 +212,9 @@ class DistributedExecutable:
             L.peers.close()
             if L.a_peers is not None:
                 L.a_peers.close()
+        if self._second is not None:
+            self._second[1].close()
+            self._second = None
         self._layers = []
         self._key = None
 
@@ -236,62 +242,135 @@ class DistributedExecutable:
         every rank of the group calls it with the same graph."""
         if self._key is None or self._key[0] != self.exe._graph_key(graph):
             self._setup(x_rows, graph)
-        rr = self._rr
-        n, dt = rr.count, self.program.feature_dtype
-        cur = torch.cuda.current_stream(self.device)
-        layers = self.program.layers
+        n = self._rr.count
         with torch.cuda.device(self.device):
             first = self._layers[0]
-            first.in_own[:n, : layers[0].in_channels].copy_(x_rows, non_blocking=True)
-            for i, (layer, L, (w, asw, adw, bias), wr) in enumerate(
-                zip(layers, self._layers, self.exe._weights, self.exe._roots, strict=True)
-            ):
-                last = i == len(layers) - 1
-                K, F = layer.in_channels, layer.width
-                gat = layer.kind == "gat"
-
-                def proj(x, rows: slice):
-                    if gat:
-                        rt.proj(x, w, att_src=asw, att_dst=adw, heads=layer.heads, out_dtype=dt,
-                                out=L.h_full[rows, :F], asrc_out=L.a_full[rows],
-                                adst_out=L.d_full[rows])
-                    else:
-                        rt.proj(x, w, out_dtype=dt, out=L.h_full[rows, :F])
-
-                own = slice(rr.begin, rr.begin + n)
-                events: list = []
-                if L.mode == "input":
-                    self._fence()  # this layer's input rows are written on every rank
-                    self._side.wait_stream(cur)
-                    with torch.cuda.stream(self._side):
-                        self._pull(L.peers, L.table, events)
-                    if n:
-                        proj(L.in_own[:n, :K], own)
-                    for rows, ev in events:
-                        cur.wait_event(ev)
-                        proj(L.table[rows, :K], rows)
-                else:
-                    if n:
-                        proj(L.in_own[:n, :K], own)
-                    self._fence()  # projected rows written everywhere
-                    self._side.wait_stream(cur)
-                    with torch.cuda.stream(self._side):
-                        self._pull(L.peers, L.h_full, events)
-                        if gat:
-                            self._pull(L.a_peers, L.a_full, events)
-                    for _, ev in events:
-                        cur.wait_event(ev)
-                if layer.kind == "sage" and n:
-                    rt.proj(L.in_own[:n, :K], wr, out_dtype=dt, out=L.root[:n, :F])
-                if last:
-                    out = self._out[:n]
-                else:
-                    nxt = self._layers[i + 1]
-                    out = nxt.in_own[:n, : layers[i + 1].in_channels]
-                if n:
-                    self._aggregate(layer, L, n, bias, out)
+            first.in_own[:n, : self.program.layers[0].in_channels].copy_(x_rows, non_blocking=True)
+            for i in range(len(self._layers)):
+                self._layer(i)
             self._fence()  # every peer is done reading this forward's rows
         return self._out[:n]
+
+    def run_stream(self, batches, graph: torch.Tensor):
+        """Forwards of a stream of batches, pipelined across them.
+
+        `batches` yields this rank's input rows of each batch (host or device
+        tensors, the rows run_device takes). When the first layer exchanges its
+        input rows, the copy engines pull batch k+1's remote input rows while
+        batch k aggregates (two input tables, each mapped by the peers), so that
+        exchange leaves the critical path; the other layers run as in
+        run_device. Yields this rank's output rows of each batch on the device,
+        valid until the next batch is requested; each equals run_device's
+        result for that batch. Collective: every rank iterates the same number
+        of batches with the same graph."""
+        it = iter(batches)
+        x = next(it, None)
+        if x is None:
+            return
+        if self._key is None or self._key[0] != self.exe._graph_key(graph):
+            self._setup(x, graph)
+        if self.world == 1 or self._layers[0].mode != "input":
+            while x is not None:
+                yield self.run_device(x, graph)
+                x = next(it, None)
+            return
+        rr, N = self._rr, self._key[1]
+        n, K0 = rr.count, self.program.layers[0].in_channels
+        L0 = self._layers[0]
+        if self._second is None:
+            t = torch.zeros_like(L0.table)
+            self._second = (t, _PeerTable(t, rr, self.group))
+        tabs = (L0.table, self._second[0])
+        peers = (L0.peers, self._second[1])
+        cur = torch.cuda.current_stream(self.device)
+        pulled = (torch.cuda.Event(), torch.cuda.Event())
+
+        def pull(b: int) -> None:
+            self._side.wait_stream(cur)
+            with torch.cuda.stream(self._side):
+                self._pull(peers[b], tabs[b], [])
+                pulled[b].record(self._side)
+
+        with torch.cuda.device(self.device):
+            tabs[0][rr.begin : rr.begin + n, :K0].copy_(x, non_blocking=True)
+            self._fence()  # batch 0's input rows are written on every rank
+            pull(0)
+            k = 0
+            while x is not None:
+                nxt = next(it, None)
+                b = k % 2
+                cur.wait_event(pulled[b])  # batch k's remote rows are present
+                if nxt is not None:
+                    # this slot's previous batch (k-1) was pulled before the last fence
+                    tabs[1 - b][rr.begin : rr.begin + n, :K0].copy_(nxt, non_blocking=True)
+                # every rank holds batch k's rows and wrote batch k+1's own rows
+                self._fence()
+                self._layer(0, table=tabs[b][:N], pull_next=(lambda: pull(1 - b))
+                            if nxt is not None else None)
+                for i in range(1, len(self._layers)):
+                    self._layer(i)
+                self._fence()  # every peer is done reading this batch's rows
+                yield self._out[:n]
+                x, k = nxt, k + 1
+
+    def _layer(self, i: int, table: torch.Tensor | None = None, pull_next=None) -> None:
+        """Layer i of a forward on the current stream: its exchange, projection
+        and aggregation into the next layer's input slot (or the output).
+        `table` is the first layer's input table with every rank's rows already
+        present (a batch of run_stream): it is projected in one launch, and
+        `pull_next` then starts the next batch's pull before the aggregation."""
+        rr, layer, L = self._rr, self.program.layers[i], self._layers[i]
+        w, asw, adw, bias = self.exe._weights[i]
+        wr = self.exe._roots[i]
+        n, dt = rr.count, self.program.feature_dtype
+        cur = torch.cuda.current_stream(self.device)
+        K, F = layer.in_channels, layer.width
+        gat = layer.kind == "gat"
+
+        def proj(x, rows: slice):
+            if gat:
+                rt.proj(x, w, att_src=asw, att_dst=adw, heads=layer.heads, out_dtype=dt,
+                        out=L.h_full[rows, :F], asrc_out=L.a_full[rows], adst_out=L.d_full[rows])
+            else:
+                rt.proj(x, w, out_dtype=dt, out=L.h_full[rows, :F])
+
+        own = slice(rr.begin, rr.begin + n)
+        x_own = L.in_own
+        events: list = []
+        if table is not None:
+            proj(table[:, :K], slice(0, table.size(0)))
+            x_own = table[rr.begin : rr.begin + rr.rows_per_rank]
+        elif L.mode == "input":
+            self._fence()  # this layer's input rows are written on every rank
+            self._side.wait_stream(cur)
+            with torch.cuda.stream(self._side):
+                self._pull(L.peers, L.table, events)
+            if n:
+                proj(L.in_own[:n, :K], own)
+            for rows, ev in events:
+                cur.wait_event(ev)
+                proj(L.table[rows, :K], rows)
+        else:
+            if n:
+                proj(L.in_own[:n, :K], own)
+            self._fence()  # projected rows written everywhere
+            self._side.wait_stream(cur)
+            with torch.cuda.stream(self._side):
+                self._pull(L.peers, L.h_full, events)
+                if gat:
+                    self._pull(L.a_peers, L.a_full, events)
+            for _, ev in events:
+                cur.wait_event(ev)
+        if layer.kind == "sage" and n:
+            rt.proj(x_own[:n, :K], wr, out_dtype=dt, out=L.root[:n, :F])
+        if pull_next is not None:
+            pull_next()
+        if i == len(self._layers) - 1:
+            out = self._out[:n]
+        else:
+            out = self._layers[i + 1].in_own[:n, : self.program.layers[i + 1].in_channels]
+        if n:
+            self._aggregate(layer, L, n, bias, out)
 
     def _aggregate(self, layer, L: _Layer, n: int, bias, out: torch.Tensor) -> None:
         N, F = self._key[1], layer.width

@@ -145,11 +145,22 @@ def _main_distributed(args) -> int:
             t = torch.tensor([s.elapsed_time(e) / args.iters], dtype=torch.float64, device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             say(f"  forward  : {float(t):.3f} ms (mean of {args.iters}, max over ranks)")
+            # the same forwards as one pipelined stream of batches
+            dist.barrier()
+            s.record()
+            for _ in dexe.run_stream((xd for _ in range(args.iters)), graph):
+                pass
+            e.record()
+            torch.cuda.synchronize(dev)
+            ts = torch.tensor([s.elapsed_time(e) / args.iters], dtype=torch.float64, device=dev)
+            dist.all_reduce(ts, op=dist.ReduceOp.MAX)
+            say(f"  stream   : {float(ts):.3f} ms per batch (run_stream: the first layer's "
+                "exchange of batch k+1 overlaps batch k)")
             if args.json and rank == 0:
                 import json
 
                 print(json.dumps({"model": args.model, "dataset": args.dataset, "gpus": world,
-                                  "forward_ms": float(t)}))
+                                  "forward_ms": float(t), "stream_ms_per_batch": float(ts)}))
         dist.barrier()
         dexe.close()
         code = 0

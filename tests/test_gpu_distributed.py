@@ -4,7 +4,8 @@ Two ranks run as two processes on cuda:0 (a gloo group with host fences; the
 CUDA IPC mappings work between processes of one device), so the test needs one
 GPU. Each rank's output rows must equal the same rows of the single-process
 executable bit for bit: every row is projected and aggregated by the same
-kernels on the same values. The models cover both exchange sides (input rows
+kernels on the same values; so must every batch of a pipelined stream
+(run_stream). The models cover both exchange sides (input rows
 for 100 -> 4x64 and 256 -> 256, projected rows for 256 -> 47), GCN, GAT and
 SAGE, bf16 features, rows split across CTAs.
 """
@@ -73,7 +74,12 @@ def _rank(rank, world, port, out_dir, model_name):
     rr = P.row_range(x.size(0), world, rank)
     outs = [dexe(x[rr.begin : rr.end], graph) for _ in range(2)]  # twice: buffers reused
     ref = exe(x, graph)[0][rr.begin : rr.end]
-    torch.save({"outs": outs, "ref": ref, "modes": modes}, os.path.join(out_dir, f"r{rank}.pt"))
+    # a stream of three different batches, the first layer's exchange pipelined
+    xs = [x, (x.float() * 0.5).to(x.dtype), -x]
+    stream = [o.cpu() for o in dexe.run_stream((xb[rr.begin : rr.end] for xb in xs), graph)]
+    stream_ref = [exe(xb, graph)[0][rr.begin : rr.end] for xb in xs]
+    torch.save({"outs": outs, "ref": ref, "modes": modes, "stream": stream,
+                "stream_ref": stream_ref}, os.path.join(out_dir, f"r{rank}.pt"))
     dist.barrier()
     dexe.close()
     dist.barrier()
@@ -94,3 +100,7 @@ def test_two_rank_forward_matches_single_process(device, tmp_path, model_name):
         for out in got["outs"]:
             assert out.shape == got["ref"].shape
             assert torch.equal(out, got["ref"]), f"rank {r}: max diff {(out - got['ref']).abs().max()}"
+        assert len(got["stream"]) == 3
+        for k, (out, ref) in enumerate(zip(got["stream"], got["stream_ref"], strict=True)):
+            assert torch.equal(out, ref), f"rank {r}, batch {k}: max diff {(out - ref).abs().max()}"
+        assert not torch.equal(got["stream"][0], got["stream"][2])
