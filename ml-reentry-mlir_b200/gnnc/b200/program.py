@@ -406,6 +406,7 @@ class B200Executable:
         self._graphs: dict[tuple, tuple[object, DeviceGraph]] = {}
         self._results = _PinnedResults()
         self._copy_stream: torch.cuda.Stream | None = None
+        self._in_stream: torch.cuda.Stream | None = None  # run_stream's input copies
         self._cuda_graphs: dict[tuple, tuple] = {}
         self.cuda_graph_error: str | None = None
 
@@ -475,7 +476,8 @@ class B200Executable:
     host_chunk_min_edges = 1 << 21
 
     def run_device(self, x: torch.Tensor, graph: torch.Tensor, events: list | None = None,
-                   host_out=None, layer_outputs: list | None = None) -> torch.Tensor:
+                   host_out=None, layer_outputs: list | None = None, staged: bool = False,
+                   host_done: list | None = None) -> torch.Tensor:
         """Forward on device-resident (or host) inputs; returns the device output.
 
         events: if a list, receives per layer a (projection_start, aggregation_start,
@@ -485,10 +487,14 @@ class B200Executable:
         host_out: if given, a callable (shape, dtype) -> page-locked host tensor;
         the result is copied into it (overlapped with the last aggregation) and
         the host tensor is returned once the copies are queued (synchronize the
-        current stream before reading it)."""
+        current stream before reading it).
+        staged: x is already a device buffer of the feature dtype with 16-byte
+        aligned rows (run_stream's input slots); it is read in place.
+        host_done: with host_out, if a list, receives an event recorded after the
+        result's copies instead of the current stream waiting for them."""
         dt = self.program.feature_dtype
         n = x.size(0)
-        h_in = to_device_features(x, dt, self.device)
+        h_in = x if staged else to_device_features(x, dt, self.device)
         layers = self.program.layers
         with torch.cuda.device(self.device):
             for i, (layer, (w, asrc_w, adst_w, bias), wr) in enumerate(
@@ -521,7 +527,8 @@ class B200Executable:
                 out = rt.empty_rows(n, width, out_dtype, self.device)
                 if last and host_out is not None:
                     host = host_out((n, width), out_dtype)
-                    self._aggregate_to_host(layer, g, h, asrc, adst, bias, out, host, root)
+                    self._aggregate_to_host(layer, g, h, asrc, adst, bias, out, host, root,
+                                            host_done)
                     h_in = host
                 else:
                     self._aggregate(layer, g, g.plan, 0, n, h, asrc, adst, bias, out, root)
@@ -549,7 +556,8 @@ class B200Executable:
                              bias=bias, act=layer.act, log_softmax=layer.log_softmax,
                              out_dtype=out.dtype, out=out[r0:r1])
 
-    def _aggregate_to_host(self, layer, g, h, asrc, adst, bias, out, host, root=None) -> None:
+    def _aggregate_to_host(self, layer, g, h, asrc, adst, bias, out, host, root=None,
+                           host_done: list | None = None) -> None:
         k = self.host_chunks if g.num_edges >= self.host_chunks * self.host_chunk_min_edges else 1
         cur = torch.cuda.current_stream(self.device)
         if self._copy_stream is None:
@@ -564,7 +572,75 @@ class B200Executable:
             with torch.cuda.stream(side):
                 host[r0:r1].copy_(out[r0:r1], non_blocking=True)
         out.record_stream(side)
-        cur.wait_stream(side)
+        if host_done is None:
+            cur.wait_stream(side)
+        else:
+            done = torch.cuda.Event()
+            done.record(side)
+            host_done.append(done)
+
+    def run_stream(self, batches, graph: torch.Tensor):
+        """Forwards of a stream of batches of host input rows, pipelined.
+
+        For callers that feed many batches through one GPU over PCIe, where a
+        call at a time leaves one copy direction idle: batch k+1's input rows
+        go to the device on one copy engine while batch k computes and its
+        result rows come back on the other (the result copies overlap the last
+        aggregation as in __call__). `batches` yields host tensors [N, in]
+        (page-locked ones copy at full rate). Yields each batch's result, a
+        page-locked host tensor as __call__ returns for host inputs, once its
+        copies completed; a result the caller keeps is never overwritten.
+        Runs eagerly (no CUDA-graph replay) and equals __call__ row for row."""
+        it = iter(batches)
+        x = next(it, None)
+        if x is None:
+            return
+        dev, dt = self.device, self.program.feature_dtype
+        cur = torch.cuda.current_stream(dev)
+        if self._in_stream is None:
+            self._in_stream = torch.cuda.Stream(dev)
+        ins = self._in_stream
+        slots: list[torch.Tensor | None] = [None, None]
+        freed: list[torch.cuda.Event | None] = [None, None]  # the slot's last forward done
+
+        def stage(x: torch.Tensor, b: int):
+            if x.is_cuda:
+                raise ValueError("run_stream takes host batches")
+            n, c = x.shape
+            buf = slots[b]
+            if buf is None or tuple(buf.shape) != (n, c):
+                buf = slots[b] = rt.empty_rows(n, c, dt, dev)
+                buf.record_stream(ins)
+            if freed[b] is not None:
+                ins.wait_event(freed[b])
+            with torch.cuda.stream(ins):
+                buf.copy_(x, non_blocking=True)
+                ready = torch.cuda.Event()
+                ready.record(ins)
+            return buf, ready
+
+        with torch.cuda.device(dev):
+            staged = stage(x, 0)
+            pending = None
+            k = 0
+            while staged is not None:
+                buf, ready = staged
+                nxt = next(it, None)
+                cur.wait_event(ready)
+                done: list = []
+                host = self.run_device(buf, graph, host_out=self._results.take, staged=True,
+                                       host_done=done)
+                ev = torch.cuda.Event()
+                ev.record(cur)
+                freed[k % 2] = ev
+                staged = stage(nxt, (k + 1) % 2) if nxt is not None else None
+                if pending is not None:
+                    pending[1].synchronize()
+                    yield pending[0]
+                pending = (host, done[0])
+                k += 1
+            pending[1].synchronize()
+            yield pending[0]
 
     def graph_edges(self, graph: torch.Tensor, num_nodes: int) -> list[int]:
         """Stored edges (self-loops included) each layer aggregates over."""
