@@ -842,6 +842,8 @@ def e2e_b200(args, layer, ei_host, x_host, device, world, N, E, project, aggrega
         # is pipelined) and the step's output rows out; the output copy runs on
         # its own stream from one of two output buffers, overlapping the next
         # step's input copy and compute
+        from gnnc.b200 import runtime as rt
+
         outs = [out_l, rt.empty_rows(lay.n_loc, F, torch.bfloat16, device)]
         out_pin = [torch.empty((lay.n_loc, F), dtype=torch.bfloat16, pin_memory=True)
                    for _ in range(2)]
