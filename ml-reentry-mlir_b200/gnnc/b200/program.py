@@ -283,6 +283,8 @@ class DeviceGraph:
     w: torch.Tensor | None  # fp32 [E] (GCN weights) or None (GAT)
     plan: rt.Plan
     num_nodes: int
+    cta_threshold: int = 0  # the plan's thresholds as given (0: the library's default)
+    split_threshold: int = 0
     _chunks: dict = field(default_factory=dict, repr=False)
 
     @property
@@ -291,14 +293,26 @@ class DeviceGraph:
 
     def row_chunks(self, k: int) -> list[tuple[int, int, rt.Plan]]:
         """The rows split into k ranges of about equal edge counts, each with its
-        own plan over the (un-rebased) rowptr slice; built once per k."""
+        own plan over the (un-rebased) rowptr slice; built once per k.
+
+        Each chunk plan splits exactly the rows the whole graph's plan splits
+        (the whole graph's split threshold, not the default a chunk's smaller
+        edge count would give), so every row takes the same kernel path and
+        the chunked result equals the single launch bit for bit."""
         got = self._chunks.get(k)
         if got is None:
+            from gnnc.b200.partition import whole_graph_split_threshold
+
             n = self.rowptr.numel() - 1
+            split = self.split_threshold or whole_graph_split_threshold(
+                self.num_edges, torch.cuda.get_device_properties(self.rowptr.device)
+                .multi_processor_count)
             targets = torch.linspace(0, self.num_edges, k + 1, device=self.rowptr.device)[1:-1]
             cuts = torch.searchsorted(self.rowptr, targets.to(torch.int32)).tolist()
             bounds = sorted({0, n, *(min(max(int(c), 0), n) for c in cuts)})
-            got = [(a, b, rt.Plan(self.rowptr[a : b + 1])) for a, b in zip(bounds, bounds[1:]) if b > a]
+            got = [(a, b, rt.Plan(self.rowptr[a : b + 1], cta_threshold=self.cta_threshold,
+                                  split_threshold=split))
+                   for a, b in zip(bounds, bounds[1:]) if b > a]
             self._chunks[k] = got
         return got
 
@@ -319,7 +333,7 @@ def graph_from_csr(adj: torch.Tensor, device, *, cta_threshold=0, split_threshol
     w = adj.values().to(device=device, dtype=torch.float32, non_blocking=True).contiguous()
     rt.validate_csr(rowptr, col, adj.size(1))
     plan = rt.Plan(rowptr, cta_threshold=cta_threshold, split_threshold=split_threshold)
-    return DeviceGraph(rowptr, col, w, plan, adj.size(0))
+    return DeviceGraph(rowptr, col, w, plan, adj.size(0), cta_threshold, split_threshold)
 
 
 def graph_from_edge_index(
@@ -342,7 +356,7 @@ def graph_from_edge_index(
     elif dedupe:
         w = mult.to(torch.float32)
     plan = rt.Plan(rowptr, cta_threshold=cta_threshold, split_threshold=split_threshold)
-    return DeviceGraph(rowptr, col, w, plan, num_nodes)
+    return DeviceGraph(rowptr, col, w, plan, num_nodes, cta_threshold, split_threshold)
 
 
 def to_device_features(x: torch.Tensor, dtype: torch.dtype, device) -> torch.Tensor:

@@ -400,6 +400,48 @@ def test_partition_plans_split_like_the_whole_graph(device):
         assert torch.equal(out, full[rr.begin : rr.end]), f"rank {r}"
 
 
+def test_host_row_chunks_split_like_the_whole_graph(device):
+    """The row chunks a host-bound result is aggregated in (DeviceGraph.row_chunks)
+    split exactly the rows the whole graph's plan splits, so the chunked rows
+    equal the single launch bit for bit; a chunk's own default threshold
+    follows its smaller edge count and would split hub rows the whole plan
+    keeps whole."""
+    from gnnc.b200 import partition as P
+    from gnnc.b200 import runtime as rt
+    from gnnc.b200.program import DeviceGraph
+
+    g = torch.Generator().manual_seed(12)
+    n = 100_000
+    deg = torch.randint(20, 80, (n,), generator=g)
+    hubs = torch.randperm(n, generator=g)[:40]
+    deg[hubs] = torch.randint(4200, 9000, (40,), generator=g)
+    rowptr = torch.zeros(n + 1, dtype=torch.int64)
+    rowptr[1:] = deg.cumsum(0)
+    E = int(rowptr[-1])
+    col = torch.randint(0, n, (E,), generator=g, dtype=torch.int32)
+    rowptr_d, col_d = rowptr.to(torch.int32).to(device), col.to(device)
+    h = torch.randn(n, 256, generator=g).to(torch.bfloat16).to(device)
+    a = (torch.randn(n, 4, generator=g) * 0.5).to(device)
+    d = (torch.randn(n, 4, generator=g) * 0.5).to(device)
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    thr = P.whole_graph_split_threshold(E, sms)
+    k = 8
+    # some hub rows lie between a chunk's own default and the whole graph's threshold
+    assert int(((deg > P.whole_graph_split_threshold(E // k, sms)) & (deg <= thr)).sum()) > 0
+    dg = DeviceGraph(rowptr_d, col_d, None, rt.Plan(rowptr_d), n)
+    whole = dg.plan.info()
+    assert whole["n_split_rows"] == int((deg > thr).sum())
+    chunks = dg.row_chunks(k)
+    assert len(chunks) == k
+    assert sum(p.info()["n_split_rows"] for _, _, p in chunks) == whole["n_split_rows"]
+    kw = dict(heads=4, concat=True, act=rt.ACT_ELU, out_dtype=torch.bfloat16)
+    full = rt.gat_aggregate(dg.plan, rowptr_d, col_d, h, a, d, **kw)
+    out = torch.empty_like(full)
+    for r0, r1, plan in chunks:
+        rt.gat_aggregate(plan, rowptr_d[r0 : r1 + 1], col_d, h, a, d[r0:r1], out=out[r0:r1], **kw)
+    assert torch.equal(out, full)
+
+
 @pytest.mark.parametrize("heads", [4, 0])
 def test_edge_stream_with_empty_rows_hubs_and_splits(device, heads):
     """The prefetched edge stream (256-wide bf16 rows, GAT and GCN modes) over
